@@ -1,0 +1,458 @@
+"""Benchmark of the B200 student-linear hot path (prints ONE JSON line on rank 0).
+
+Workload (N = 1 GPU): BASELINE config 1 -- all 168 FP8 linears of a random-init
+Qwen2.5-0.5B-shaped model, 512 tokens each, codebook student: per-token e4m3
+quantisation, the exact int64 GEMM (tcgen05 kind::i8, fused rescale/bias/bf16
+epilogue) with full int64 outputs, and a Freivalds check of every product.
+A "step" is one forward of all 168 linears.  Metric: exact int GEMM TOPS =
+sum over linears of 2*M*N*K / step time (whole job, all GPUs).
+
+N > 1 (torchrun): every rank runs the same workload on its own token batch (weak
+scaling); the only collective is an all-reduce of the Freivalds mismatch counter.
+
+--impl reference times the reference's CPU path (its torch expressions: per-token
+quantiser, torch int64 matmul, fp32 rescale) on the host cores over a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TOKENS = 512
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_int8_peak(device) -> float:
+    """Dense int8 tensor throughput of a library GEMM (torch._int_mm, 8192^3), TOPS."""
+    n = 8192
+    a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device=device)
+    b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device=device).t().contiguous().t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    del a, b
+    return 2 * n**3 / (best * 1e-3) / 1e12
+
+
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def profile_traffic(name: str) -> float | None:
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>.md."""
+    path = os.path.join(ROOT, "profiles", f"{name}.md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        return None
+    return None
+
+
+def build_workload(config: int, tokens: int, device, rank: int):
+    from int_model_approximation_b200 import synthetic
+
+    shapes = synthetic.config_linears(config)
+    weights, xs = [], []
+    for i, s in enumerate(shapes):
+        seed = synthetic.linear_seed(config, i)
+        w, ws = synthetic.normal_fp8_weights(s.n, s.k, seed + 500_000, device=device)
+        g = torch.Generator(device=device).manual_seed(seed + 77)
+        bias = (torch.randn(s.n, generator=g, device=device) * 0.01).to(torch.bfloat16)
+        weights.append((w, ws, bias))
+        xs.append(synthetic.student_t_activations(tokens, s.k, seed + 1_000_003 * rank, device=device,
+                                                  outlier_fraction=synthetic.CONFIGS[config]["outliers"]))
+    return shapes, weights, xs
+
+
+def run_b200(args) -> None:
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    from int_model_approximation_b200 import _native as nat
+    from int_model_approximation_b200.pipeline import CodebookStack
+
+    nat.lib()
+    int8_peak = measured_int8_peak(device)
+    shapes, weights, xs = build_workload(1, TOKENS, device, rank)
+    stack = CodebookStack(weights, seed=rank)
+    bufs = stack.allocate(TOKENS)
+    flops = sum(2.0 * TOKENS * s.n * s.k for s in shapes)
+
+    # eager warm-up (initialises kernel attributes, tensor-map entry points)
+    stack.forward(xs, bufs)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        stack.forward(xs, bufs)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            stack.forward(xs, bufs)
+    # GEMM-only graph (for the roofline of the dominant kernel)
+    gemm_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(gemm_graph, stream=stream):
+            _launch_gemms_only(stack, bufs, TOKENS)
+    torch.cuda.synchronize()
+
+    def step():
+        graph.replay()
+        if world > 1:
+            torch.distributed.all_reduce(bufs["mismatch"])
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    bufs["mismatch"].zero_()
+
+    # ---- timed region (device resident inputs; inputs 2.4 GB per step > L2) ----
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        s_ev.record(stream)
+        for _ in range(args.steps):
+            step()
+        e_ev.record(stream)
+    e_ev.synchronize()
+    clocks = sampler.stop()
+    ms = s_ev.elapsed_time(e_ev) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    mismatches = int(bufs["mismatch"].item())
+
+    # ---- dominant kernel: the GEMMs alone, same stream, CUDA events ----
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            gemm_graph.replay()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            gemm_graph.replay()
+        g1.record(stream)
+    g1.synchronize()
+    gemm_ms_per_step = g0.elapsed_time(g1) / args.steps
+    gemm_launches = len(shapes)
+
+    # ---- end to end through the public API: host buffers in, host results out ----
+    host_x = [x.cpu().pin_memory() for x in xs]
+    host_y = [torch.empty(y.shape, dtype=y.dtype).pin_memory() for y in bufs["y"]]
+    host_mm = torch.empty((1,), dtype=torch.int32).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in host_x)
+    d2h = sum(y.numel() * y.element_size() for y in host_y) + 4
+    with torch.cuda.stream(stream):
+        def e2e_step():
+            for hx, dx in zip(host_x, xs):
+                dx.copy_(hx, non_blocking=True)
+            step()
+            for hy, dy in zip(host_y, bufs["y"]):
+                hy.copy_(dy, non_blocking=True)
+            host_mm.copy_(bufs["mismatch"], non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        x1.record(stream)
+    x1.synchronize()
+    e2e_ms = x0.elapsed_time(x1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(shapes, weights, xs, budget_s=args.cpu_seconds)
+
+    if rank == 0:
+        peaks = measured_peaks()
+        total_ops = flops * world
+        value = total_ops / (ms * 1e-3) / 1e12
+        # Karatsuba: six int8 plane products per exact product
+        gemm_tc_ops = 6.0 * flops / (gemm_ms_per_step * 1e-3) / 1e12
+        traffic = profile_traffic("int_gemm_c1")
+        line = {
+            "metric": "exact int GEMM TOPS (bit-exact codebook int64 GEMM + fused rescale + Freivalds check)",
+            "value": round(value, 3),
+            "unit": "TOPS",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int8 digit planes -> int32 TMEM -> int64",
+            "data": "synthetic (seeded Student-t activations, N(0,0.02) e4m3 weights; no checkpoint)",
+            "config": {
+                "workload": "c1: 168 FP8 linears of Qwen2.5-0.5B shape, 512 tokens per GPU, codebook student, "
+                            "int64 outputs + per-linear Freivalds",
+                "linears": len(shapes),
+                "tokens_per_gpu": TOKENS,
+                "exact_int_ops_per_step_per_gpu": flops,
+                "l2": "inputs larger than L2 (about 2.4 GB of weight planes and activations per step)",
+                "launch": "one CUDA graph per step",
+                "parallelism": f"replicas x{world} (token batches per rank)",
+            },
+            "freivalds_mismatch_rows": mismatches,
+            "gpu_launches": len(shapes) * 4 * args.steps,
+            "roofline": {
+                "kernel": "int_gemm_kernel<KARATSUBA3>",
+                "bound": "tensor",
+                "achieved": round(gemm_tc_ops, 2),
+                "peak": round(int8_peak, 1),
+                "unit": "TOPS (int8 tensor ops, 6 plane products per exact product)",
+                "frac": round(gemm_tc_ops / int8_peak, 4),
+                "peak_source": "torch._int_mm 8192^3 best-of-10 measured in this run (MEASURED_PEAKS.json has no int8 figure)",
+                "traffic": traffic,
+                "gemm_ms_per_step": round(gemm_ms_per_step, 4),
+                "gemm_launches_per_step": gemm_launches,
+                "exact_tops_gemm_only": round(flops / (gemm_ms_per_step * 1e-3) / 1e12, 3),
+            },
+            "e2e": {
+                "value": round(total_ops / (e2e_ms * 1e-3) / 1e12, 3),
+                "unit": "TOPS",
+                "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "api": "CodebookStack.forward (bf16 activations from pinned host memory, bf16 outputs + "
+                       "Freivalds verdict back to host)",
+            },
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "measured_peaks": {k: peaks.get(k) for k in ("hbm_gbs", "bf16_tflops")},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del graph, gemm_graph
+        torch.distributed.destroy_process_group()
+
+
+def _launch_gemms_only(stack, bufs, tokens):
+    from int_model_approximation_b200 import _native as nat
+
+    lib = nat.lib()
+    stream = nat.stream_of(stack.device)
+    for i, lin in enumerate(stack.linears):
+        planes = bufs["planes"][i]
+        nat.check("ima_int_gemm", lib.ima_int_gemm(
+            planes.planes.data_ptr(), planes.ld, lin.w_planes.planes.data_ptr(), lin.w_planes.ld, tokens, lin.n,
+            lin.k, nat.IMA_SCHEME_KARATSUBA3, bufs["c"][i].data_ptr(), lin.n, bufs["code_scale"][i].data_ptr(),
+            lin.w_code_scale.data_ptr(), nat.ptr(lin.bias), bufs["y"][i].data_ptr(), nat.IMA_DTYPE_BF16, lin.n,
+            stream))
+
+
+def cpu_baseline_sample(shapes, weights, xs, budget_s: float = 15.0) -> dict:
+    """The reference's CPU path (oracle port: torch quantiser, torch int64 matmul,
+    fp32 rescale) on a bounded sample of the same workload: whole linears, cycling
+    through the model, until the time budget is used."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    done_ops, t_used, linears = 0.0, 0.0, 0
+    cpu_w = {}
+    i = 0
+    while t_used < budget_s and linears < len(shapes):
+        s = shapes[i]
+        w, ws, bias = weights[i]
+        if i not in cpu_w:
+            cpu_w[i] = (w.cpu(), ws.cpu(), bias.cpu())
+        x = xs[i].cpu()
+        wc, wsc, bc = cpu_w[i]
+        t0 = time.perf_counter()
+        oracle.torch_cpu_codebook_linear(x, wc, wsc, bc)
+        t_used += time.perf_counter() - t0
+        done_ops += 2.0 * x.shape[0] * s.n * s.k
+        linears += 1
+        i += 1
+    return {
+        "value": round(done_ops / t_used / 1e12, 6),
+        "unit": "TOPS",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{linears} whole linears of the c1 workload ({TOKENS} tokens each), {t_used:.1f} s of CPU time",
+    }
+
+
+def run_reference(args) -> None:
+    world, rank, _local = _dist()
+    if rank != 0:
+        return
+    from int_model_approximation_b200 import synthetic
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    shapes = synthetic.config_linears(1)
+    rows = args.reference_rows
+
+    def sample(i):
+        s = shapes[i % len(shapes)]
+        seed = synthetic.linear_seed(1, i % len(shapes))
+        x = synthetic.student_t_activations(rows, s.k, seed)
+        w, ws = synthetic.normal_fp8_weights(s.n, s.k, seed + 500_000)
+        return s, x, w, ws
+
+    for i in range(args.warmup):
+        s, x, w, ws = sample(i)
+        oracle.torch_cpu_codebook_linear(x, w, ws, None)
+    total_t, total_ops = 0.0, 0.0
+    for i in range(args.steps):
+        s, x, w, ws = sample(args.warmup + i)
+        t0 = time.perf_counter()
+        oracle.torch_cpu_codebook_linear(x, w, ws, None)
+        total_t += time.perf_counter() - t0
+        total_ops += 2.0 * rows * s.n * s.k
+    value = total_ops / total_t / 1e12
+    line = {
+        "impl": "reference",
+        "metric": "exact int GEMM TOPS (bit-exact codebook int64 GEMM + fused rescale + Freivalds check)",
+        "value": round(value, 6),
+        "unit": "TOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_t / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int64",
+        "data": "synthetic",
+        "config": {"workload": "c1: 168 FP8 linears of Qwen2.5-0.5B shape, codebook student",
+                   "sample_rows_per_step": rows},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+                         "sample": f"one linear per step, {rows} token rows, cycling through the 168 linears"},
+        "e2e": {"value": round(value, 6), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--reference-rows", type=int, default=64)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

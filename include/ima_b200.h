@@ -1,0 +1,150 @@
+/*
+ * ima_b200.h -- C ABI of the B200-native student-linear hot path of
+ * int-model-approximation (codebook exact int GEMM, direct Hawkeye replay,
+ * Hawkeye class-count products, Freivalds check).
+ *
+ * Conventions
+ *   - Plain device pointers, 64-bit sizes and leading dimensions in ELEMENTS,
+ *     and a cudaStream_t passed as void*.  No framework types.
+ *   - Every entry point returns an int status (IMA_OK == 0).  Argument checks
+ *     happen before any launch; kernels never trap: a device-side failure (a
+ *     bounded wait that ran out, an index outside a tensor) is recorded in a
+ *     per-device status word read by ima_device_status().
+ *   - Launches are asynchronous on the given stream; no entry point
+ *     synchronises unless its comment says so.
+ *   - "ref:" cites the reference interface each entry point replaces, as
+ *     path:line inside the reference package src/int_model_approximation/.
+ */
+#ifndef IMA_B200_H
+#define IMA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------- */
+#define IMA_OK 0
+#define IMA_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, bad leading dim */
+#define IMA_ERR_UNSUPPORTED 2      /* parameter value the B200 kernels do not implement */
+#define IMA_ERR_CUDA 3             /* a CUDA runtime call or launch failed */
+#define IMA_ERR_TIMEOUT 4          /* device: a bounded wait ran out */
+#define IMA_ERR_DEVICE_BOUNDS 5    /* device: an index fell outside a tensor */
+#define IMA_ERR_OVERFLOW 6         /* operand magnitude outside the exact range of the scheme */
+
+/* element types for untyped buffers */
+#define IMA_DTYPE_F32 0
+#define IMA_DTYPE_BF16 1
+#define IMA_DTYPE_F16 2
+
+/* ---- runtime -------------------------------------------------------------- */
+int ima_abi_version(void);                 /* bumped on any signature change */
+const char* ima_status_string(int status); /* static string, never NULL */
+int ima_last_cuda_error(void);             /* cudaError_t of the last failing CUDA call (this thread) */
+
+/* Reads (synchronously: waits for the device) and optionally clears the device status
+ * word of `device`.  code == IMA_OK when no kernel recorded a failure. */
+int ima_device_status(int device, int* code, int* where, int* detail, int clear);
+
+/* ---- A1/A2: per-token FP8 quantiser -----------------------------------------
+ * ref: __main__.py:148-154 _per_token_fp8, :157-158 _fp8_e4m3_to_int32,
+ *      :161-163 _per_token_fp8_int32.
+ * x [M,K] (dtype IMA_DTYPE_*, row stride ldx) ->
+ *   q_fp8 [M,K] e4m3 bytes (row stride ldq),
+ *   scale [M] fp32 = max(amax_row|x| / 448, 1e-12),
+ *   codebook [M,K] int32 = round(q * 512) (optional, row stride ldc),
+ *   code_scale [M] fp32 = scale / 512 (optional),
+ *   planes [6][M][ldp] int8: the six Karatsuba digit planes of the codebook
+ *   values used by ima_int_gemm (optional; ldp >= K, multiple of 16; columns
+ *   K..ldp-1 are written as zero). */
+int ima_quantize_per_token(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, uint8_t* q_fp8,
+                           int64_t ldq, float* scale, int32_t* codebook, int64_t ldc, float* code_scale,
+                           int8_t* planes, int64_t ldp, void* stream);
+
+/* Exact codebook values round(fp8 * 512) of an e4m3 matrix [rows,K] into int32 [rows,K]
+ * (row stride ldd).  ref: __main__.py:157-158 _fp8_e4m3_to_int32.  NaN codes give 0,
+ * like CUDA's float->int32 conversion of NaN in the reference expression. */
+int ima_codebook_from_fp8(const uint8_t* src, int64_t rows, int64_t K, int64_t ld, int32_t* dst, int64_t ldd,
+                          void* stream);
+
+/* Karatsuba digit planes of a matrix of e4m3 bytes ([rows,K], row stride ld), e.g. the
+ * weight of a CodebookLinear (ref: __main__.py:429-432, done once per linear).
+ * codebook_t [K,rows] int32 (optional) receives the transposed codebook the reference
+ * keeps as `weight_t`. */
+int ima_planes_from_fp8(const uint8_t* src, int64_t rows, int64_t K, int64_t ld, int8_t* planes, int64_t ldp,
+                        int32_t* codebook_t, void* stream);
+
+/* Digit planes of an int32 matrix given by element strides (stride_row, stride_k), so that
+ * both the activation layout [M,K] and the reference's weight_t layout [K,N] can be
+ * expanded.  scheme: IMA_SCHEME_KARATSUBA3 (|v| <= 1064960) or IMA_SCHEME_DIGITS5 (any
+ * int32).  Values outside the scheme's range set the device status to IMA_ERR_OVERFLOW. */
+#define IMA_SCHEME_KARATSUBA3 3
+#define IMA_SCHEME_DIGITS5 5
+int ima_planes_from_int32(const int32_t* src, int64_t rows, int64_t K, int64_t stride_row, int64_t stride_k,
+                          int scheme, int8_t* planes, int64_t ldp, void* stream);
+int ima_scheme_planes(int scheme); /* number of planes a scheme uses (6 or 5) */
+
+/* Largest |v| over an int32 matrix (device reduction into *out_maxabs, a device int64
+ * the caller zeroes).  Used to choose the digit scheme of _int32_matmul. */
+int ima_int32_maxabs(const int32_t* src, int64_t rows, int64_t cols, int64_t stride_row, int64_t stride_col,
+                     int64_t* out_maxabs, void* stream);
+
+/* ---- A3: exact int32 x int32 -> int64 GEMM on tcgen05 kind::i8 tensor cores ----
+ * ref: __main__.py:188-253 _int32_raw_matmul (c only) and :256-333 _int32_matmul
+ *      (y = (fp32_rn(C) * x_scale[m]) * w_scale[n]).
+ * a_planes: [P][M][lda] int8, b_planes: [P][N][ldb] int8 (both K-major), P =
+ * ima_scheme_planes(scheme).  Outputs (each optional, at least one):
+ *   c [M,N] int64 (row stride ldc), exact modulo 2^64 like the reference's int64
+ *   accumulator;
+ *   y [M,N] of y_dtype (row stride ldy) = (fp32_rn(C) * x_scale[m]) * w_scale[n]
+ *   (+ bias[n] in fp32 when bias != NULL), rounded once to y_dtype.
+ * x_scale / w_scale may be NULL only when y == NULL. */
+int ima_int_gemm(const int8_t* a_planes, int64_t lda, const int8_t* b_planes, int64_t ldb, int64_t M, int64_t N,
+                 int64_t K, int scheme, int64_t* c, int64_t ldc, const float* x_scale, const float* w_scale,
+                 const float* bias, void* y, int y_dtype, int64_t ldy, void* stream);
+
+/* ---- A4: direct Hawkeye replay ---------------------------------------------
+ * ref: hawkeye.py:222-275 hawkeye_fp8_sum (kernel hawkeye.py:127-219).
+ * Each operand (activations and weights alike) is first staged once with
+ * ima_hawkeye_prepare into a buffer of ima_hawkeye_operand_bytes(rows, K) bytes.
+ * Replay supports products_per_group == 32, internal_width == 14,
+ * zero_exponent == -139 (IMA_ERR_UNSUPPORTED otherwise).
+ * out_bf16 [M,N] (bf16 bits) and/or out_f32 [M,N]: (gfloat * x_scale[m]) * w_scale[n]. */
+int64_t ima_hawkeye_operand_pitch(int64_t rows);
+int64_t ima_hawkeye_operand_bytes(int64_t rows, int64_t K);
+int ima_hawkeye_prepare(const uint8_t* fp8, int64_t rows, int64_t K, int64_t ld, void* operand, void* stream);
+int ima_hawkeye_replay(const void* x_operand, const void* w_operand, const float* x_scale, const float* w_scale,
+                       int64_t M, int64_t N, int64_t K, int products_per_group, int internal_width,
+                       int zero_exponent, uint16_t* out_bf16, int64_t ld_bf16, float* out_f32, int64_t ld_f32,
+                       void* stream);
+
+/* ---- A6: Freivalds check A (B r) == (A B) r, wrapping int64 ------------------
+ * ref: tests/test_real_integer_gemms.py:67-93 (_exact_matvec /
+ *      _assert_freivalds_verifies_int_product; the reference has no production API).
+ * Adds to *mismatch_rows (device int32, the caller zeroes it) the number of rows m with
+ * sum_k A[m,k] (sum_n B[k,n] r[n]) != sum_n C[m,n] r[n] (mod 2^64).
+ * workspace: device buffer of ima_freivalds_workspace_bytes(K) bytes. */
+int64_t ima_freivalds_workspace_bytes(int64_t K);
+/* A = codebook(x_fp8) [M,K], B = codebook(w_fp8)^T with w_fp8 [N,K] (CodebookLinear's operands) */
+int ima_freivalds_fp8(const uint8_t* x_fp8, int64_t ldx, const uint8_t* w_fp8, int64_t ldw, const int64_t* c,
+                      int64_t ldc, const int64_t* r, int64_t M, int64_t N, int64_t K, void* workspace,
+                      int32_t* mismatch_rows, void* stream);
+/* A int32 [M,K] (row stride lda), B int32 [K,N] (row stride ldb; the reference's weight_t) */
+int ima_freivalds_i32(const int32_t* a, int64_t lda, const int32_t* b, int64_t ldb, const int64_t* c, int64_t ldc,
+                      const int64_t* r, int64_t M, int64_t N, int64_t K, void* workspace, int32_t* mismatch_rows,
+                      void* stream);
+
+/* ---- A5: Hawkeye class counts -----------------------------------------------
+ * ref: hawkeye_freivalds.py:51-57 _class_ids; the per-pack class sets the reference
+ * builds with torch.unique (hawkeye_freivalds.py:906-907, :1097-1098).
+ * masks [packs][16] uint32 (packs = ceil(K / pack_width)): bit c of pack p is set iff
+ * class id c occurs in columns [p*pack_width, (p+1)*pack_width) of any row. */
+int ima_class_presence(const uint8_t* fp8, int64_t rows, int64_t K, int64_t ld, int64_t pack_width, uint32_t* masks,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IMA_B200_H */

@@ -1,0 +1,150 @@
+"""ctypes binding of libima_b200.so (the C ABI declared in include/ima_b200.h).
+
+This is the only place Python touches the native library.  There is no CPU or
+PyTorch fallback: if the library is missing, every entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_native", "libima_b200.so")
+_LOCK = threading.Lock()
+_LIB: ctypes.CDLL | None = None
+
+IMA_OK = 0
+IMA_ERR_INVALID_ARGUMENT = 1
+IMA_ERR_UNSUPPORTED = 2
+IMA_ERR_CUDA = 3
+IMA_ERR_TIMEOUT = 4
+IMA_ERR_DEVICE_BOUNDS = 5
+IMA_ERR_OVERFLOW = 6
+
+IMA_DTYPE_F32 = 0
+IMA_DTYPE_BF16 = 1
+IMA_DTYPE_F16 = 2
+
+IMA_SCHEME_KARATSUBA3 = 3
+IMA_SCHEME_DIGITS5 = 5
+
+_VP = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int
+
+# name -> (restype, argtypes); mirrors include/ima_b200.h
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "ima_abi_version": (_I32, []),
+    "ima_status_string": (ctypes.c_char_p, [_I32]),
+    "ima_last_cuda_error": (_I32, []),
+    "ima_device_status": (_I32, [_I32, _VP, _VP, _VP, _I32]),
+    "ima_quantize_per_token": (
+        _I32,
+        [_VP, _I32, _I64, _I64, _I64, _VP, _I64, _VP, _VP, _I64, _VP, _VP, _I64, _VP],
+    ),
+    "ima_codebook_from_fp8": (_I32, [_VP, _I64, _I64, _I64, _VP, _I64, _VP]),
+    "ima_class_presence": (_I32, [_VP, _I64, _I64, _I64, _I64, _VP, _VP]),
+    "ima_planes_from_fp8": (_I32, [_VP, _I64, _I64, _I64, _VP, _I64, _VP, _VP]),
+    "ima_planes_from_int32": (_I32, [_VP, _I64, _I64, _I64, _I64, _I32, _VP, _I64, _VP]),
+    "ima_scheme_planes": (_I32, [_I32]),
+    "ima_int32_maxabs": (_I32, [_VP, _I64, _I64, _I64, _I64, _VP, _VP]),
+    "ima_int_gemm": (
+        _I32,
+        [_VP, _I64, _VP, _I64, _I64, _I64, _I64, _I32, _VP, _I64, _VP, _VP, _VP, _VP, _I32, _I64, _VP],
+    ),
+    "ima_hawkeye_operand_pitch": (_I64, [_I64]),
+    "ima_hawkeye_operand_bytes": (_I64, [_I64, _I64]),
+    "ima_hawkeye_prepare": (_I32, [_VP, _I64, _I64, _I64, _VP, _VP]),
+    "ima_hawkeye_replay": (
+        _I32,
+        [_VP, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _I32, _I32, _VP, _I64, _VP, _I64, _VP],
+    ),
+    "ima_freivalds_workspace_bytes": (_I64, [_I64]),
+    "ima_freivalds_fp8": (
+        _I32,
+        [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP],
+    ),
+    "ima_freivalds_i32": (
+        _I32,
+        [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP],
+    ),
+}
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the native library; raise if it is not built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            if not os.path.exists(_LIB_PATH):
+                raise RuntimeError(
+                    f"the B200 kernel library {_LIB_PATH} is not built; "
+                    "run `python -c 'import __graft_entry__ as g; g.build()'` (there is no CPU execution path)"
+                )
+            handle = ctypes.CDLL(_LIB_PATH)
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _LIB = handle
+    return _LIB
+
+
+class NativeError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int):
+        self.status = status
+        text = lib().ima_status_string(status).decode()
+        detail = ""
+        if status == IMA_ERR_CUDA:
+            detail = f" (cudaError {lib().ima_last_cuda_error()})"
+        super().__init__(f"{fn} failed: {text}{detail}")
+
+
+def check(fn: str, status: int) -> None:
+    if status != IMA_OK:
+        raise NativeError(fn, status)
+
+
+def call(fn: str, *args) -> None:
+    check(fn, getattr(lib(), fn)(*args))
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_status(device: int = 0, clear: bool = True) -> tuple[int, int, int]:
+    """(code, where, detail) of the device status word; synchronises the device."""
+    code, where, detail = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    check(
+        "ima_device_status",
+        lib().ima_device_status(
+            device, ctypes.byref(code), ctypes.byref(where), ctypes.byref(detail), 1 if clear else 0
+        ),
+    )
+    return code.value, where.value, detail.value
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return IMA_DTYPE_F32
+    if dtype == torch.bfloat16:
+        return IMA_DTYPE_BF16
+    if dtype == torch.float16:
+        return IMA_DTYPE_F16
+    raise RuntimeError(f"unsupported dtype {dtype}; expected float32, bfloat16 or float16")

@@ -1,0 +1,50 @@
+// Runtime plumbing of the C ABI: status strings, the CUDA error of the last call
+// and the per-device status word.
+#include "ima_common.cuh"
+
+static thread_local int g_last_cuda_error = 0;
+
+int ima_note_cuda(cudaError_t e) {
+    if (e == cudaSuccess) return IMA_OK;
+    g_last_cuda_error = (int)e;
+    return IMA_ERR_CUDA;
+}
+
+extern "C" {
+
+int ima_abi_version(void) { return 1; }
+
+const char* ima_status_string(int status) {
+    switch (status) {
+        case IMA_OK: return "ok";
+        case IMA_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case IMA_ERR_UNSUPPORTED: return "unsupported parameter";
+        case IMA_ERR_CUDA: return "CUDA error";
+        case IMA_ERR_TIMEOUT: return "device wait timed out";
+        case IMA_ERR_DEVICE_BOUNDS: return "device index out of bounds";
+        case IMA_ERR_OVERFLOW: return "operand outside the exact range of the digit scheme";
+        default: return "unknown status";
+    }
+}
+
+int ima_last_cuda_error(void) { return g_last_cuda_error; }
+
+int ima_device_status(int device, int* code, int* where, int* detail, int clear) {
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess) return ima_note_cuda(cudaGetLastError());
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) return ima_note_cuda(cudaGetLastError());
+    ImaDeviceStatus st;
+    int rc = ima_note_cuda(cudaMemcpyFromSymbol(&st, g_ima_status, sizeof(st)));
+    if (rc == IMA_OK && clear) {
+        ImaDeviceStatus zero = {0, 0, 0, 0};
+        rc = ima_note_cuda(cudaMemcpyToSymbol(g_ima_status, &zero, sizeof(zero)));
+    }
+    if (prev != device) cudaSetDevice(prev);
+    if (rc != IMA_OK) return rc;
+    if (code) *code = st.code;
+    if (where) *where = st.where;
+    if (detail) *detail = st.detail;
+    return IMA_OK;
+}
+
+}  // extern "C"

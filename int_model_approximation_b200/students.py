@@ -1,0 +1,380 @@
+"""IMA_STUDENT_KERNEL plugin surface on B200 (drop-in for the student side of the
+reference's __main__.py).
+
+Same module-level configuration (env vars read at import, __main__.py:39-50), the
+same student modules (CodebookLinear, HawkeyeLinear, HawkeyeClassCountsLinear and
+the non-FP8 Int32Linear, __main__.py:390-523), the same kernel wrappers
+(_int32_raw_matmul :228-253, _int32_matmul :301-333), the same probe
+(_Int32KernelProbe :667-678, bumped once per checkable integer product) and the
+same replacement pass (_replace_int32_linears :563-588).  Every integer product
+runs on the sm_100a kernels of libima_b200.so; there is no CPU execution path.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+from typing import Any
+
+import torch
+import torch.nn as nn
+
+from . import _native as nat
+from .codebook import DigitPlanes, codebook_planes_from_fp8, int_gemm, per_token_fp8, planes_from_int32
+from .hawkeye import hawkeye_fp8_sum, stage_weight
+from .hawkeye_freivalds import exact_hawkeye_fp8_sum
+
+STUDENT_KERNEL = os.environ.get("IMA_STUDENT_KERNEL", "codebook")
+SUPPORTED_STUDENT_KERNELS = {"codebook", "hawkeye", "hawkeye-class-counts"}
+HAWKEYE_PRODUCTS_PER_GROUP = int(os.environ.get("IMA_HAWKEYE_GROUP", "32"))
+HAWKEYE_INTERNAL_WIDTH = int(os.environ.get("IMA_HAWKEYE_WIDTH", "14"))
+HAWKEYE_CLASS_CHUNK = int(os.environ.get("IMA_HAWKEYE_CLASS_CHUNK", "32"))
+HAWKEYE_PACKED_COUNT_LANES = int(os.environ.get("IMA_HAWKEYE_PACKED_COUNT_LANES", "6"))
+HAWKEYE_PACKED_GROUP_LANES = int(os.environ.get("IMA_HAWKEYE_PACKED_GROUP_LANES", "1"))
+HAWKEYE_ZERO_EXPONENT = -139
+HAWKEYE_BLOCK_M = int(os.environ.get("IMA_HAWKEYE_BLOCK_M", "4"))
+HAWKEYE_BLOCK_N = int(os.environ.get("IMA_HAWKEYE_BLOCK_N", "32"))
+
+FP8_E4M3_MAX = 448.0
+FP8_E4M3_CODE_SCALE = 512.0
+INT32_MAX = (1 << 31) - 1
+INT64_ACCUM_LIMIT = (1 << 62) - 1
+_ACTIVE_INT32_PROBE = None
+
+_PLANES_ATTR = "_ima_planes"
+
+
+def _require_cuda_tensor(x: torch.Tensor, label: str) -> None:
+    if x.device.type != "cuda":
+        raise RuntimeError(f"{label} must be on CUDA; this repo has no CPU execution path")
+
+
+def _attach_planes(t: torch.Tensor, planes: DigitPlanes) -> None:
+    try:
+        setattr(t, _PLANES_ATTR, (planes, t._version))
+    except (AttributeError, RuntimeError):
+        pass
+
+
+def _attached_planes(t: torch.Tensor) -> DigitPlanes | None:
+    entry = getattr(t, _PLANES_ATTR, None)
+    if entry is None:
+        return None
+    planes, version = entry
+    return planes if version == t._version else None
+
+
+# ---------------------------------------------------------------------------
+# quantisers (ref __main__.py:148-185)
+# ---------------------------------------------------------------------------
+def _per_token_fp8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda_tensor(x, "FP8 activation")
+    q, scale, _cb, _cs, _dp = per_token_fp8(x)
+    return q, scale
+
+
+def _fp8_e4m3_to_int32(x: torch.Tensor) -> torch.Tensor:
+    _require_cuda_tensor(x, "FP8 codebook source")
+    raw = x.contiguous().view(torch.uint8)
+    shape = raw.shape
+    rows = raw.reshape(-1, shape[-1]) if raw.ndim > 1 else raw.reshape(1, -1)
+    out = torch.empty(rows.shape, dtype=torch.int32, device=raw.device)
+    with torch.cuda.device(raw.device):
+        nat.call(
+            "ima_codebook_from_fp8", rows.data_ptr(), rows.shape[0], rows.shape[1], rows.shape[1], out.data_ptr(),
+            rows.shape[1], nat.stream_of(raw.device),
+        )
+    return out.reshape(shape)
+
+
+def _per_token_fp8_int32(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda_tensor(x, "FP8 activation")
+    _q, _scale, codebook, code_scale, planes = per_token_fp8(x, codebook=True, planes=True)
+    _attach_planes(codebook, planes)
+    return codebook, code_scale
+
+
+def _int32_qmax(k: int) -> float:
+    # Keep worst-case sum_k(qmax*qmax) inside signed int64 with headroom.
+    return float(min(INT32_MAX, int(math.sqrt(INT64_ACCUM_LIMIT / max(k, 1)))))
+
+
+def _per_token_int32(x: torch.Tensor, qmax: float) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda_tensor(x, "int32 activation")
+    rows = x.reshape(-1, x.shape[-1])
+    scale = rows.detach().abs().amax(dim=-1, keepdim=True).to(torch.float32)
+    scale = (scale / qmax).clamp_min(1e-12)
+    q = (rows.to(torch.float32) / scale).round().clamp(-qmax, qmax)
+    return q.to(torch.int32).contiguous(), scale
+
+
+def _per_row_int32(weight: torch.Tensor, qmax: float) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda_tensor(weight, "int32 weight source")
+    w = weight.detach().to(torch.float32)
+    scale = (w.abs().amax(dim=1, keepdim=True) / qmax).clamp_min(1e-12)
+    q = (w / scale).round().clamp(-qmax, qmax)
+    return q.to(torch.int32).contiguous(), scale.to(torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# integer GEMM wrappers (ref __main__.py:228-333)
+# ---------------------------------------------------------------------------
+def _operand_planes(activations: torch.Tensor, weight_t: torch.Tensor) -> tuple[DigitPlanes, DigitPlanes]:
+    a = _attached_planes(activations)
+    b = _attached_planes(weight_t)
+    if a is not None and b is not None and a.scheme == b.scheme:
+        return a, b
+    # Unknown int32 values: the five-digit scheme is exact for every int32.
+    if a is None or a.scheme != nat.IMA_SCHEME_DIGITS5:
+        a = planes_from_int32(activations, scheme=nat.IMA_SCHEME_DIGITS5)
+    if b is None or b.scheme != nat.IMA_SCHEME_DIGITS5:
+        b = planes_from_int32(weight_t, transpose=True, scheme=nat.IMA_SCHEME_DIGITS5)
+    return a, b
+
+
+def _int32_raw_matmul(activations: torch.Tensor, weight_t: torch.Tensor) -> torch.Tensor:
+    global _ACTIVE_INT32_PROBE
+    _require_cuda_tensor(activations, "int32 activation matrix")
+    _require_cuda_tensor(weight_t, "int32 weight matrix")
+    if activations.dtype != torch.int32 or weight_t.dtype != torch.int32:
+        raise RuntimeError("int32 raw matmul received non-int32 operands")
+    m_size, k_size = activations.shape
+    k2, n_size = weight_t.shape
+    if k_size != k2:
+        raise RuntimeError(f"int32 raw matmul shape mismatch: {activations.shape} @ {weight_t.shape}")
+    out = torch.empty((m_size, n_size), device=activations.device, dtype=torch.int64)
+    if _ACTIVE_INT32_PROBE is not None:
+        _ACTIVE_INT32_PROBE.count += 1
+    a, b = _operand_planes(activations, weight_t)
+    int_gemm(a, b, c_out=out)
+    return out
+
+
+def _int32_matmul(
+    activations: torch.Tensor,
+    weight_t: torch.Tensor,
+    x_scale: torch.Tensor,
+    w_scale: torch.Tensor,
+) -> torch.Tensor:
+    global _ACTIVE_INT32_PROBE
+    _require_cuda_tensor(activations, "int32 activation matrix")
+    _require_cuda_tensor(weight_t, "int32 weight matrix")
+    if activations.dtype != torch.int32 or weight_t.dtype != torch.int32:
+        raise RuntimeError("int32 matmul received non-int32 operands")
+    m_size, k_size = activations.shape
+    k2, n_size = weight_t.shape
+    if k_size != k2:
+        raise RuntimeError(f"int32 matmul shape mismatch: {activations.shape} @ {weight_t.shape}")
+    out = torch.empty((m_size, n_size), device=activations.device, dtype=torch.float32)
+    if _ACTIVE_INT32_PROBE is not None:
+        _ACTIVE_INT32_PROBE.count += 1
+    a, b = _operand_planes(activations, weight_t)
+    int_gemm(a, b, want_c=False, x_scale=x_scale, w_scale=w_scale, y_out=out)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# student modules (ref __main__.py:390-523)
+# ---------------------------------------------------------------------------
+class Int32Linear(nn.Module):
+    """Linear backed by the exact int32 tensor-core GEMM (non-FP8 linears)."""
+
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor | None):
+        super().__init__()
+        _require_cuda_tensor(weight, "int32 weight source")
+        self.qmax = _int32_qmax(weight.shape[1])
+        w_i32, w_scale = _per_row_int32(weight, self.qmax)
+        self.register_buffer("weight_t", w_i32.t().contiguous(), persistent=False)
+        self.register_buffer("weight_scale", w_scale.reshape(1, -1), persistent=False)
+        if bias is None:
+            self.bias = None
+        else:
+            self.register_buffer("bias", bias.detach(), persistent=False)
+        self.in_features = weight.shape[1]
+        self.out_features = weight.shape[0]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _require_cuda_tensor(x, "int32 input")
+        in_shape = x.shape
+        x_i32, x_scale = _per_token_int32(x, self.qmax)
+        y = _int32_matmul(x_i32, self.weight_t, x_scale, self.weight_scale)
+        if self.bias is not None:
+            y = y + self.bias.to(torch.float32)
+        return y.to(x.dtype).reshape(*in_shape[:-1], self.out_features)
+
+
+class CodebookLinear(nn.Module):
+    """FP8 linear reconstructed by one Freivalds-checkable codebook integer GEMM."""
+
+    def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None):
+        super().__init__()
+        if weight.dtype != torch.float8_e4m3fn:
+            raise RuntimeError(f"CodebookLinear needs FP8 weights, got {weight.dtype}")
+        _require_cuda_tensor(weight, "FP8 codebook weight")
+        planes, codebook_t = codebook_planes_from_fp8(weight.detach(), with_codebook_t=True)
+        codebook_scale = weight_scale.detach().to(torch.float32) / FP8_E4M3_CODE_SCALE
+        self.register_buffer("weight_t", codebook_t, persistent=False)
+        self.register_buffer("weight_scale", codebook_scale.reshape(1, -1), persistent=False)
+        _attach_planes(self.weight_t, planes)
+        if bias is None:
+            self.bias = None
+        else:
+            self.register_buffer("bias", bias.detach(), persistent=False)
+        self.in_features = weight.shape[1]
+        self.out_features = weight.shape[0]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _require_cuda_tensor(x, "FP8 codebook input")
+        in_shape = x.shape
+        x_i32, x_scale = _per_token_fp8_int32(x)
+        y = _int32_matmul(x_i32, self.weight_t, x_scale, self.weight_scale)
+        if self.bias is not None:
+            y = y + self.bias.to(torch.float32)
+        return y.to(x.dtype).reshape(*in_shape[:-1], self.out_features)
+
+
+class HawkeyeLinear(nn.Module):
+    """FP8 linear reconstructed by direct Hawkeye integer replay."""
+
+    def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None):
+        super().__init__()
+        if weight.dtype != torch.float8_e4m3fn:
+            raise RuntimeError(f"HawkeyeLinear needs FP8 weights, got {weight.dtype}")
+        _require_cuda_tensor(weight, "Hawkeye FP8 weight")
+        self.register_buffer("weight", weight.detach().contiguous(), persistent=False)
+        self.register_buffer("weight_scale", weight_scale.detach().to(torch.float32), persistent=False)
+        stage_weight(self.weight)
+        if bias is None:
+            self.bias = None
+        else:
+            self.register_buffer("bias", bias.detach(), persistent=False)
+        self.in_features = weight.shape[1]
+        self.out_features = weight.shape[0]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _require_cuda_tensor(x, "Hawkeye input")
+        in_shape = x.shape
+        x_fp8, x_scale = _per_token_fp8(x)
+        y, _stats = hawkeye_fp8_sum(
+            x_fp8,
+            x_scale,
+            self.weight,
+            self.weight_scale,
+            products_per_group=HAWKEYE_PRODUCTS_PER_GROUP,
+            internal_width=HAWKEYE_INTERNAL_WIDTH,
+            zero_exponent=HAWKEYE_ZERO_EXPONENT,
+            block_m=HAWKEYE_BLOCK_M,
+            block_n=HAWKEYE_BLOCK_N,
+        )
+        if self.bias is not None:
+            y = y + self.bias.to(y.dtype)
+        return y.to(x.dtype).reshape(*in_shape[:-1], self.out_features)
+
+
+class HawkeyeClassCountsLinear(nn.Module):
+    """FP8 linear reconstructed exactly from checkable Hawkeye class-count products."""
+
+    def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None):
+        super().__init__()
+        if weight.dtype != torch.float8_e4m3fn:
+            raise RuntimeError(f"HawkeyeClassCountsLinear needs FP8 weights, got {weight.dtype}")
+        _require_cuda_tensor(weight, "Hawkeye exact FP8 weight")
+        self.register_buffer("weight", weight.detach().contiguous(), persistent=False)
+        self.register_buffer("weight_scale", weight_scale.detach().to(torch.float32), persistent=False)
+        stage_weight(self.weight)
+        if bias is None:
+            self.bias = None
+        else:
+            self.register_buffer("bias", bias.detach(), persistent=False)
+        self.in_features = weight.shape[1]
+        self.out_features = weight.shape[0]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _require_cuda_tensor(x, "Hawkeye exact input")
+        in_shape = x.shape
+        x_fp8, x_scale = _per_token_fp8(x)
+        y, _stats = exact_hawkeye_fp8_sum(
+            x_fp8,
+            x_scale,
+            self.weight,
+            self.weight_scale,
+            _int32_raw_matmul,
+            products_per_group=HAWKEYE_PRODUCTS_PER_GROUP,
+            internal_width=HAWKEYE_INTERNAL_WIDTH,
+            zero_exponent=HAWKEYE_ZERO_EXPONENT,
+            class_chunk=HAWKEYE_CLASS_CHUNK,
+            packed_count_lanes=HAWKEYE_PACKED_COUNT_LANES,
+            packed_group_lanes=HAWKEYE_PACKED_GROUP_LANES,
+        )
+        if self.bias is not None:
+            y = y + self.bias.to(y.dtype)
+        return y.to(x.dtype).reshape(*in_shape[:-1], self.out_features)
+
+
+# ---------------------------------------------------------------------------
+# model integerisation (ref __main__.py:526-594)
+# ---------------------------------------------------------------------------
+def _expanded_block_scale(weight: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    if scale.shape == weight.shape:
+        return scale
+    row_block = math.ceil(weight.shape[0] / scale.shape[0])
+    col_block = math.ceil(weight.shape[1] / scale.shape[1])
+    return scale.repeat_interleave(row_block, 0).repeat_interleave(col_block, 1)[
+        : weight.shape[0], : weight.shape[1]
+    ]
+
+
+def _dequantized_weight(module: nn.Linear) -> torch.Tensor:
+    weight = module.weight.detach()
+    if weight.dtype == torch.float8_e4m3fn:
+        if hasattr(module, "weight_scale"):
+            return weight.to(torch.float32) * module.weight_scale.detach().to(torch.float32)
+        if hasattr(module, "weight_scale_inv"):
+            scale = module.weight_scale_inv.detach().to(torch.float32)
+            return weight.to(torch.float32) * _expanded_block_scale(weight, scale)
+        raise RuntimeError("FP8 Linear is missing a recognized weight scale")
+    return weight.to(torch.float32)
+
+
+def _replace_int32_linears(model: nn.Module) -> list[str]:
+    if STUDENT_KERNEL not in SUPPORTED_STUDENT_KERNELS:
+        supported = ", ".join(sorted(SUPPORTED_STUDENT_KERNELS))
+        raise RuntimeError(f"unknown IMA_STUDENT_KERNEL={STUDENT_KERNEL!r}; choose one of: {supported}")
+    replacements: list[tuple[str, nn.Linear]] = []
+    for name, module in model.named_modules():
+        if isinstance(module, nn.Linear):
+            replacements.append((name, module))
+    for name, module in replacements:
+        if module.weight.dtype == torch.float8_e4m3fn and hasattr(module, "weight_scale"):
+            if STUDENT_KERNEL == "hawkeye":
+                replacement = HawkeyeLinear(module.weight, module.weight_scale, module.bias)
+            elif STUDENT_KERNEL == "hawkeye-class-counts":
+                replacement = HawkeyeClassCountsLinear(module.weight, module.weight_scale, module.bias)
+            else:
+                replacement = CodebookLinear(module.weight, module.weight_scale, module.bias)
+        else:
+            replacement = Int32Linear(_dequantized_weight(module), module.bias)
+        _set_submodule(model, name, replacement)
+    if not replacements:
+        raise RuntimeError("No Linear modules were found to integerize.")
+    return [name for name, _ in replacements]
+
+
+def _set_submodule(model: nn.Module, name: str, replacement: nn.Module) -> None:
+    parent_name, _, child_name = name.rpartition(".")
+    parent = model.get_submodule(parent_name) if parent_name else model
+    setattr(parent, child_name, replacement)
+
+
+class _Int32KernelProbe:
+    def __init__(self):
+        self.count = 0
+
+    def __enter__(self) -> "_Int32KernelProbe":
+        global _ACTIVE_INT32_PROBE
+        _ACTIVE_INT32_PROBE = self
+        return self
+
+    def __exit__(self, exc_type: Any, exc: Any, tb: Any) -> None:
+        global _ACTIVE_INT32_PROBE
+        _ACTIVE_INT32_PROBE = None

@@ -1,0 +1,321 @@
+"""GPU parity: every kernel of libima_b200.so against the CPU oracle and the
+reference's own fixtures.  Integer and bf16 outputs are compared bit for bit."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from int_model_approximation_b200 import _native as nat
+from int_model_approximation_b200 import codebook, freivalds, hawkeye, hawkeye_freivalds, students, synthetic
+from tests.conftest import golden_cases, json_field, load_golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _fp8(b: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(b)).to(device).view(torch.float8_e4m3fn)
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy()
+    if t.dtype == torch.float32:
+        return t.view(torch.int32).numpy()
+    return t.numpy()
+
+
+def _assert_status_clean(device):
+    code, where, detail = nat.device_status(device.index or 0)
+    assert code == 0, f"device status {code} at {where}/{detail}"
+
+
+# ---------------------------------------------------------------------------
+# quantiser
+# ---------------------------------------------------------------------------
+def test_quantiser_matches_reference_fixture(cuda_device):
+    g = load_golden("quantize")
+    x = torch.from_numpy(g["x_bf16"].view(np.int16)).view(torch.bfloat16).to(cuda_device)
+    q, scale, cb, cs, planes = codebook.per_token_fp8(x, codebook=True, planes=True)
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), g["q"])
+    assert np.array_equal(_bits(scale), g["scale"].view(np.int32))
+    assert np.array_equal(cb.cpu().numpy(), g["codebook"])
+    assert np.array_equal(_bits(cs), g["code_scale"].view(np.int32))
+    x32 = torch.from_numpy(g["x_f32"]).to(cuda_device)
+    q32, s32, *_ = codebook.per_token_fp8(x32)
+    assert np.array_equal(q32.view(torch.uint8).cpu().numpy(), g["q_f32"])
+    assert np.array_equal(_bits(s32), g["scale_f32"].view(np.int32))
+
+
+def test_e4m3_conversion_sweep(cuda_device):
+    """Rows whose amax is exactly 448 have scale 1, so the kernel's cast of every
+    in-range fixture value is compared with torch's cast directly."""
+    g = load_golden("e4m3_cast")
+    f = g["f32"]
+    f = f[np.abs(f) <= 448.0]
+    pad = (-len(f)) % 255
+    f = np.concatenate([f, np.zeros(pad, dtype=np.float32)]).reshape(-1, 255)
+    rows = np.concatenate([np.full((f.shape[0], 1), 448.0, dtype=np.float32), f], axis=1)
+    x = torch.from_numpy(rows).to(cuda_device)
+    q, scale, *_ = codebook.per_token_fp8(x)
+    assert torch.all(scale == 1.0)
+    expect = torch.from_numpy(rows).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), expect)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_quantiser_random_rows_against_oracle(cuda_device, dtype):
+    x = synthetic.student_t_activations(37, 1000, seed=3, outlier_fraction=0.01, dtype=dtype)
+    x[5] = 0
+    q, scale, cb, _cs, _ = codebook.per_token_fp8(x.to(cuda_device), codebook=True)
+    q_ref, s_ref = oracle.per_token_fp8(x)
+    assert torch.equal(q.view(torch.uint8).cpu(), q_ref.view(torch.uint8))
+    assert torch.equal(scale.cpu(), s_ref)
+    assert torch.equal(cb.cpu(), oracle.fp8_codebook(q_ref))
+
+
+# ---------------------------------------------------------------------------
+# Hawkeye replay
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("case", sorted(golden_cases(load_golden("hawkeye")).keys()))
+def test_hawkeye_matches_reference_fixture(cuda_device, case):
+    d = golden_cases(load_golden("hawkeye"))[case]
+    x, w = _fp8(d["x"], cuda_device), _fp8(d["w"], cuda_device)
+    xs = torch.from_numpy(d["x_scale"]).to(cuda_device)
+    ws = torch.from_numpy(d["w_scale"]).to(cuda_device)
+    out, stats = hawkeye.hawkeye_fp8_sum(x, xs, w, ws)
+    assert np.array_equal(_bits(out), d["exact_bf16"].view(np.int16))
+    f32 = torch.empty(out.shape, dtype=torch.float32, device=cuda_device)
+    hawkeye.hawkeye_replay(hawkeye.HawkeyeOperand(x), hawkeye.HawkeyeOperand(w), xs, ws, out_f32=f32)
+    assert np.array_equal(_bits(f32), d["y_f32"].view(np.int32))
+    assert stats.total_checkable_products == 0
+    assert stats.groups == (x.shape[1] + 31) // 32
+    _assert_status_clean(cuda_device)
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 32, 1), (5, 31, 7), (65, 100, 129), (130, 257, 300), (16, 896, 4864)])
+def test_hawkeye_random_shapes_against_oracle(cuda_device, m, k, n):
+    x = synthetic.student_t_activations(m, k, seed=m + k, outlier_fraction=0.01)
+    xq, xs = oracle.per_token_fp8(x)
+    w, ws = synthetic.normal_fp8_weights(n, k, seed=n + k)
+    out, _ = hawkeye.hawkeye_fp8_sum(xq.to(cuda_device), xs.to(cuda_device), w.to(cuda_device), ws.to(cuda_device))
+    ref = oracle.hawkeye(xq, xs, w, ws).to(torch.bfloat16)
+    assert torch.equal(out.cpu().view(torch.int16), ref.view(torch.int16))
+
+
+def test_hawkeye_raw_byte_patterns_against_oracle(cuda_device):
+    g = torch.Generator().manual_seed(9)
+    x = torch.randint(0, 256, (70, 160), generator=g, dtype=torch.int64).to(torch.uint8).view(torch.float8_e4m3fn)
+    w = torch.randint(0, 256, (90, 160), generator=g, dtype=torch.int64).to(torch.uint8).view(torch.float8_e4m3fn)
+    xs = torch.rand(70, 1, generator=g) + 0.25
+    ws = torch.rand(90, generator=g) + 0.25
+    out, _ = hawkeye.hawkeye_fp8_sum(x.to(cuda_device), xs.to(cuda_device), w.to(cuda_device), ws.to(cuda_device))
+    ref = oracle.hawkeye(x, xs, w, ws).to(torch.bfloat16)
+    assert torch.equal(out.cpu().view(torch.int16), ref.view(torch.int16))
+
+
+def test_hawkeye_c2_shape_sampled_rows(cuda_device):
+    """Config-2 shape (M = 16384 tokens, gate_proj) with 0.1% outliers: sampled rows are
+    exact checks because every output row is independent."""
+    x, w, ws = synthetic.make_linear_inputs(2, 4, synthetic.LinearShape("gate_proj", 4864, 896), device=cuda_device)
+    xq, xs, *_ = codebook.per_token_fp8(x)
+    out, _ = hawkeye.hawkeye_fp8_sum(xq, xs, w, ws)
+    rows = torch.randperm(x.shape[0], generator=torch.Generator().manual_seed(0))[:24].numpy()
+    ref = oracle.hawkeye(xq.cpu(), xs.cpu(), w.cpu(), ws.cpu(), rows=rows).to(torch.bfloat16)
+    assert torch.equal(out[torch.from_numpy(rows).to(cuda_device)].cpu().view(torch.int16), ref.view(torch.int16))
+
+
+# ---------------------------------------------------------------------------
+# exact int GEMM (tcgen05)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("case", ["ref_test_4x3", "c16x96x40", "c7x200x33", "c3x32x17"])
+def test_codebook_linear_matches_reference_fixture(cuda_device, case):
+    d = golden_cases(load_golden("codebook"))[case]
+    x = torch.from_numpy(d["x"]).to(cuda_device)
+    if bool(d["x_is_bf16"]):
+        x = x.to(torch.bfloat16)
+    w = _fp8(d["w"], cuda_device)
+    ws = torch.from_numpy(d["w_scale"]).to(cuda_device)
+    bias = None
+    if "bias_bf16" in d:
+        bias = torch.from_numpy(d["bias_bf16"].view(np.int16)).view(torch.bfloat16).to(cuda_device)
+    layer = students.CodebookLinear(w, ws, bias)
+    x_i32, x_scale = students._per_token_fp8_int32(x)
+    with students._Int32KernelProbe() as probe:
+        c = students._int32_raw_matmul(x_i32, layer.weight_t)
+        y = students._int32_matmul(x_i32, layer.weight_t, x_scale, layer.weight_scale)
+        out = layer(x)
+    assert probe.count == 3
+    assert np.array_equal(c.cpu().numpy(), d["c"])
+    assert np.array_equal(_bits(y), d["y"].view(np.int32))
+    assert np.array_equal(_bits(out.to(torch.float32)), d["out_f32"].view(np.int32))
+    _assert_status_clean(cuda_device)
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1, 1), (3, 17, 5), (128, 128, 64), (129, 300, 65), (512, 896, 4864),
+                                   (200, 4864, 896), (77, 18944, 40)])
+def test_int_gemm_codebook_against_oracle(cuda_device, m, k, n):
+    x = synthetic.student_t_activations(m, k, seed=m * 7 + k)
+    w, ws = synthetic.normal_fp8_weights(n, k, seed=n * 3 + k)
+    xq, xs, *_ = codebook.per_token_fp8(x.to(cuda_device), planes=True)
+    _, _, _, _, a = codebook.per_token_fp8(x.to(cuda_device), planes=True)
+    b, _ = codebook.codebook_planes_from_fp8(w.to(cuda_device))
+    c, y = codebook.int_gemm(a, b, x_scale=xs / 512.0, w_scale=ws.to(cuda_device) / 512.0, y_dtype=torch.float32)
+    rows = np.arange(m) if m <= 256 else np.random.default_rng(0).choice(m, 96, replace=False)
+    a_ref = oracle.fp8_codebook(xq.cpu())[torch.from_numpy(rows)]
+    b_ref = oracle.fp8_codebook(w)
+    c_ref = oracle.int_gemm(a_ref, b_ref, b_is_nk=True)
+    assert torch.equal(c.cpu()[torch.from_numpy(rows)], c_ref)
+    y_ref = oracle.rescale(c_ref, (xs.cpu() / 512.0)[torch.from_numpy(rows)], ws / 512.0)
+    assert torch.equal(y.cpu()[torch.from_numpy(rows)].view(torch.int32), y_ref.view(torch.int32))
+    _assert_status_clean(cuda_device)
+
+
+def test_int_gemm_extreme_codebook_values(cuda_device):
+    """All operands at the largest codebook magnitude (0x7E = 448 -> 229376): the
+    largest possible |C| for this K, exact in int64."""
+    k = 4864
+    x = torch.full((130, k), 0x7E, dtype=torch.uint8)
+    x[::2] = 0xFE
+    w = torch.full((70, k), 0x7E, dtype=torch.uint8)
+    w[:, ::3] = 0xFE
+    a, _ = codebook.codebook_planes_from_fp8(x.view(torch.float8_e4m3fn).to(cuda_device))
+    b, _ = codebook.codebook_planes_from_fp8(w.view(torch.float8_e4m3fn).to(cuda_device))
+    c, _ = codebook.int_gemm(a, b)
+    ref = oracle.int_gemm(oracle.fp8_codebook(x.view(torch.float8_e4m3fn)), oracle.fp8_codebook(w.view(torch.float8_e4m3fn)),
+                          b_is_nk=True)
+    assert torch.equal(c.cpu(), ref)
+
+
+@pytest.mark.parametrize("lo,hi", [(-(2**31), 2**31), (-1000, 1000)])
+def test_int32_raw_matmul_generic_int32(cuda_device, lo, hi):
+    g = torch.Generator().manual_seed(hi % 1000)
+    a = torch.randint(lo, hi, (70, 200), generator=g, dtype=torch.int64).to(torch.int32)
+    b = torch.randint(lo, hi, (200, 45), generator=g, dtype=torch.int64).to(torch.int32)
+    a[0, :] = -(2**31) if lo < -1000 else lo
+    c = students._int32_raw_matmul(a.to(cuda_device), b.to(cuda_device))
+    assert torch.equal(c.cpu(), oracle.int_gemm(a, b))
+
+
+def test_raw_int32_matmul_is_freivalds_verifiable(cuda_device):
+    """The reference's prime-matrix test (tests/test_real_integer_gemms.py:252-278)."""
+    g = load_golden("freivalds")
+    a = torch.from_numpy(g["prime_a"]).to(cuda_device)
+    b = torch.from_numpy(g["prime_b"]).to(cuda_device)
+    c = students._int32_raw_matmul(a, b)
+    assert c.dtype == torch.int64 and c.device.type == "cuda"
+    assert np.array_equal(c.cpu().numpy(), g["prime_c"])
+    for r in g["prime_vectors"]:
+        rt = torch.from_numpy(r).to(cuda_device)
+        assert freivalds.verify_int32_product(a, b, c, rt)
+        assert oracle.exact_matvec(a.cpu().tolist(), oracle.exact_matvec(b.cpu().tolist(), r.tolist())) == \
+            oracle.exact_matvec(c.cpu().tolist(), r.tolist())
+    bad = c.clone()
+    bad[0, 0] += 1
+    assert not freivalds.verify_int32_product(a, b, bad, torch.from_numpy(g["prime_vectors"][0]).to(cuda_device))
+
+
+# ---------------------------------------------------------------------------
+# Freivalds
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("m,k,n", [(1, 5, 3), (33, 300, 70), (512, 896, 4864), (64, 4864, 896)])
+def test_freivalds_codebook_accepts_and_rejects(cuda_device, m, k, n):
+    x = synthetic.student_t_activations(m, k, seed=k + 1)
+    w, ws = synthetic.normal_fp8_weights(n, k, seed=k + 2)
+    xq, xs, *_ = codebook.per_token_fp8(x.to(cuda_device))
+    a = codebook.per_token_fp8(x.to(cuda_device), planes=True)[4]
+    b, _ = codebook.codebook_planes_from_fp8(w.to(cuda_device))
+    c, _ = codebook.int_gemm(a, b)
+    r = freivalds.freivalds_vector(n, seed=k + 7, device=cuda_device)
+    wd = w.to(cuda_device)
+    assert freivalds.verify_codebook_product(xq, wd, c, r)
+    bad = c.clone()
+    bad[m // 2, n // 3] += 1
+    assert int(r[n // 3]) != 0
+    assert int(freivalds.mismatch_rows_codebook(xq, wd, bad, r).item()) == 1
+    # oracle agrees on the verdicts
+    a_ref = oracle.fp8_codebook(xq.cpu())
+    b_ref = oracle.fp8_codebook(w).t().contiguous()
+    assert oracle.freivalds_mismatch_rows(a_ref, b_ref, c.cpu(), r.cpu()) == 0
+    assert oracle.freivalds_mismatch_rows(a_ref, b_ref, bad.cpu(), r.cpu()) == 1
+
+
+# ---------------------------------------------------------------------------
+# class counts
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("case", [c for c in sorted(golden_cases(load_golden("class_counts")).keys()) if c != "packing"])
+def test_class_counts_match_reference_fixture(cuda_device, case):
+    d = golden_cases(load_golden("class_counts"))[case]
+    params = json_field(d["params"])
+    x, w = _fp8(d["x"], cuda_device), _fp8(d["w"], cuda_device)
+    with students._Int32KernelProbe() as probe:
+        y, stats = hawkeye_freivalds.exact_hawkeye_fp8_sum(
+            x, torch.ones((x.shape[0], 1), device=cuda_device), w, torch.ones((w.shape[0],), device=cuda_device),
+            students._int32_raw_matmul, **params,
+        )
+    assert np.array_equal(_bits(y), d["y_bf16"].view(np.int16))
+    assert stats.__dict__ == json_field(d["stats"])
+    assert probe.count == stats.total_checkable_products
+
+
+def test_class_counts_c3_shape_against_direct_and_oracle(cuda_device):
+    """Config 3: down_proj M=4096, K=4864, N=896, chunk 512, 6 lanes, 2 group lanes."""
+    x, w, ws = synthetic.make_linear_inputs(3, 0, synthetic.LinearShape("down_proj", 896, 4864), device=cuda_device)
+    xq, xs, *_ = codebook.per_token_fp8(x)
+    y, stats = hawkeye_freivalds.exact_hawkeye_fp8_sum(
+        xq, xs, w, ws, students._int32_raw_matmul, class_chunk=512, packed_count_lanes=6, packed_group_lanes=2
+    )
+    direct, _ = hawkeye.hawkeye_fp8_sum(xq, xs, w, ws)
+    assert torch.equal(y.view(torch.int16), direct.view(torch.int16))
+    rows = np.arange(0, 4096, 331)
+    ref = oracle.hawkeye(xq.cpu(), xs.cpu(), w.cpu(), ws.cpu(), rows=rows).to(torch.bfloat16)
+    assert torch.equal(y[torch.from_numpy(rows).to(cuda_device)].cpu().view(torch.int16), ref.view(torch.int16))
+    assert stats.__dict__ == oracle.class_count_stats(xq.cpu(), w.cpu(), class_chunk=512, packed_count_lanes=6,
+                                                       packed_group_lanes=2)
+    assert stats.groups == 152
+
+
+# ---------------------------------------------------------------------------
+# the plugin surface end to end
+# ---------------------------------------------------------------------------
+def _fp8_model(device):
+    model = torch.nn.Sequential(torch.nn.Linear(96, 64, bias=True), torch.nn.GELU(), torch.nn.Linear(64, 40))
+    for i, lin in enumerate((model[0], model[2])):
+        w, ws = synthetic.normal_fp8_weights(lin.out_features, lin.in_features, seed=90 + i)
+        lin.weight = torch.nn.Parameter(w, requires_grad=False)
+        lin.weight_scale = ws
+    return model.to(device)
+
+
+@pytest.mark.parametrize("kernel", ["codebook", "hawkeye", "hawkeye-class-counts"])
+def test_student_model_end_to_end(cuda_device, monkeypatch, kernel):
+    monkeypatch.setattr(students, "STUDENT_KERNEL", kernel)
+    model = _fp8_model(cuda_device)
+    w0 = model[0].weight.detach().cpu().clone()
+    ws0 = model[0].weight_scale.detach().cpu().clone()
+    b0 = model[0].bias.detach().cpu().clone()
+    replaced = students._replace_int32_linears(model)
+    assert replaced == ["0", "2"]
+    x = synthetic.student_t_activations(9, 96, seed=5).to(cuda_device)
+    with torch.inference_mode(), students._Int32KernelProbe() as probe:
+        y = model(x)
+        torch.cuda.synchronize()
+    assert y.shape == (9, 40)
+    if kernel == "codebook":
+        assert probe.count == 2
+    elif kernel == "hawkeye":
+        assert probe.count == 0
+    else:
+        assert probe.count > 0
+    with torch.inference_mode():
+        h = model[0](x)
+    if kernel == "codebook":
+        ref = oracle.codebook_linear(x.cpu(), w0, ws0, b0)[2]
+    else:
+        xq, xs = oracle.per_token_fp8(x.cpu())
+        ref = oracle.hawkeye(xq, xs, w0, ws0).to(torch.bfloat16)
+        ref = (ref + b0.to(torch.bfloat16)).to(x.dtype)
+    assert torch.equal(h.cpu().view(torch.int16), ref.view(torch.int16))
