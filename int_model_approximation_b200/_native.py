@@ -124,6 +124,18 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def require_device(device: torch.device, *named: tuple[str, torch.Tensor | None]) -> None:
+    """Refuse (before any launch) tensors that are not on `device`: a host or
+    other-device pointer must never reach a kernel."""
+    for label, t in named:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise RuntimeError(f"{label} must be on CUDA; this repo has no CPU execution path")
+        if t.device != device:
+            raise RuntimeError(f"{label} is on {t.device}, expected {device}")
+
+
 def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 

@@ -166,6 +166,14 @@ def int_gemm(
         w_scale = w_scale.reshape(-1).to(torch.float32).contiguous()
         if bias is not None:
             bias = bias.reshape(-1).to(torch.float32).contiguous()
+        if x_scale.numel() != m or w_scale.numel() != n or (bias is not None and bias.numel() != n):
+            raise RuntimeError(
+                f"int_gemm scale/bias sizes {x_scale.numel()}, {w_scale.numel()} do not match M={m}, N={n}"
+            )
+    nat.require_device(
+        dev, ("B planes", b.planes), ("int64 output", c), ("output", y), ("x_scale", x_scale),
+        ("w_scale", w_scale), ("bias", bias),
+    )
     with torch.cuda.device(dev):
         nat.call(
             "ima_int_gemm",

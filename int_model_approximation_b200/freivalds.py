@@ -53,6 +53,7 @@ def mismatch_rows_codebook(
     dev = c.device
     if out is None:
         out = torch.zeros((1,), dtype=torch.int32, device=dev)
+    nat.require_device(dev, ("product", c), ("activations", x), ("weights", w), ("vector", r), ("counter", out))
     ws = _workspace(k, dev)
     with torch.cuda.device(dev):
         nat.call(
@@ -87,6 +88,7 @@ def mismatch_rows_int32(
     dev = c.device
     if out is None:
         out = torch.zeros((1,), dtype=torch.int32, device=dev)
+    nat.require_device(dev, ("product", c), ("a", a), ("b", b), ("vector", r), ("counter", out))
     ws = _workspace(k, dev)
     with torch.cuda.device(dev):
         nat.call(

@@ -99,8 +99,14 @@ def hawkeye_replay(
     dev = x_op.device
     xs = x_scale.reshape(-1).to(torch.float32).contiguous()
     ws = w_scale.reshape(-1).to(torch.float32).contiguous()
+    if xs.numel() != m or ws.numel() != n:
+        raise RuntimeError(f"Hawkeye scales have {xs.numel()} and {ws.numel()} entries, expected {m} and {n}")
+    if w_op.k != k:
+        raise RuntimeError(f"Hawkeye shape mismatch: K={k} vs K={w_op.k}")
     if out is None and out_f32 is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    nat.require_device(dev, ("weight operand", w_op.buffer), ("x_scale", xs), ("w_scale", ws), ("output", out),
+                       ("fp32 output", out_f32))
     with torch.cuda.device(dev):
         nat.call(
             "ima_hawkeye_replay",

@@ -49,9 +49,20 @@ def _require_cuda_tensor(x: torch.Tensor, label: str) -> None:
         raise RuntimeError(f"{label} must be on CUDA; this repo has no CPU execution path")
 
 
-def _attach_planes(t: torch.Tensor, planes: DigitPlanes) -> None:
+def _version_of(t: torch.Tensor) -> int | None:
+    # Inference tensors (torch.inference_mode) carry no version counter.
     try:
-        setattr(t, _PLANES_ATTR, (planes, t._version))
+        return t._version
+    except RuntimeError:
+        return None
+
+
+def _attach_planes(t: torch.Tensor, planes: DigitPlanes) -> None:
+    """Remember the digit planes of an int32 operand on the tensor object itself, so that
+    _int32_matmul can skip re-expanding it; the planes are used only while the tensor's
+    version counter is unchanged (inference tensors have none and are taken as is)."""
+    try:
+        setattr(t, _PLANES_ATTR, (planes, _version_of(t)))
     except (AttributeError, RuntimeError):
         pass
 
@@ -61,7 +72,7 @@ def _attached_planes(t: torch.Tensor) -> DigitPlanes | None:
     if entry is None:
         return None
     planes, version = entry
-    return planes if version == t._version else None
+    return planes if version == _version_of(t) else None
 
 
 # ---------------------------------------------------------------------------

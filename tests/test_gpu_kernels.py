@@ -283,11 +283,31 @@ def test_class_counts_c3_shape_against_direct_and_oracle(cuda_device):
 # ---------------------------------------------------------------------------
 def _fp8_model(device):
     model = torch.nn.Sequential(torch.nn.Linear(96, 64, bias=True), torch.nn.GELU(), torch.nn.Linear(64, 40))
+    model = model.to(device)
     for i, lin in enumerate((model[0], model[2])):
         w, ws = synthetic.normal_fp8_weights(lin.out_features, lin.in_features, seed=90 + i)
-        lin.weight = torch.nn.Parameter(w, requires_grad=False)
-        lin.weight_scale = ws
-    return model.to(device)
+        lin.weight = torch.nn.Parameter(w.to(device), requires_grad=False)
+        lin.weight_scale = ws.to(device)   # a plain attribute, as compressed-tensors checkpoints expose it
+    return model
+
+
+def test_host_tensors_are_refused_before_launch(cuda_device):
+    w, ws = synthetic.normal_fp8_weights(40, 64, seed=1)
+    layer = students.CodebookLinear(w.to(cuda_device), ws, None)   # scale left on the host
+    x = synthetic.student_t_activations(3, 64, seed=2).to(cuda_device)
+    with pytest.raises(RuntimeError, match="must be on CUDA"):
+        layer(x)
+    torch.cuda.synchronize()
+
+
+def test_inference_mode_keeps_the_codebook_scheme(cuda_device):
+    w, ws = synthetic.normal_fp8_weights(40, 64, seed=1)
+    layer = students.CodebookLinear(w.to(cuda_device), ws.to(cuda_device), None)
+    x = synthetic.student_t_activations(3, 64, seed=2).to(cuda_device)
+    with torch.inference_mode():
+        x_i32, _ = students._per_token_fp8_int32(x)
+        a, b = students._operand_planes(x_i32, layer.weight_t)
+    assert a.scheme == b.scheme == nat.IMA_SCHEME_KARATSUBA3
 
 
 @pytest.mark.parametrize("kernel", ["codebook", "hawkeye", "hawkeye-class-counts"])
