@@ -124,6 +124,14 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def tensor_version(t: torch.Tensor) -> int | None:
+    """The tensor's in-place version counter (None for inference tensors, which have none)."""
+    try:
+        return t._version
+    except RuntimeError:
+        return None
+
+
 def require_device(device: torch.device, *named: tuple[str, torch.Tensor | None]) -> None:
     """Refuse (before any launch) tensors that are not on `device`: a host or
     other-device pointer must never reach a kernel."""

@@ -51,10 +51,10 @@ class HawkeyeOperand:
                 nat.stream_of(raw.device),
             )
         self._source = fp8
-        self._version = fp8._version
+        self._version = nat.tensor_version(fp8)
 
     def matches(self, fp8: torch.Tensor) -> bool:
-        return fp8 is self._source and fp8._version == self._version
+        return fp8 is self._source and nat.tensor_version(fp8) == self._version
 
 
 def _validate_params(products_per_group: int, internal_width: int, zero_exponent: int) -> None:

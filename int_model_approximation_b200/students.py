@@ -49,12 +49,7 @@ def _require_cuda_tensor(x: torch.Tensor, label: str) -> None:
         raise RuntimeError(f"{label} must be on CUDA; this repo has no CPU execution path")
 
 
-def _version_of(t: torch.Tensor) -> int | None:
-    # Inference tensors (torch.inference_mode) carry no version counter.
-    try:
-        return t._version
-    except RuntimeError:
-        return None
+_version_of = nat.tensor_version
 
 
 def _attach_planes(t: torch.Tensor, planes: DigitPlanes) -> None:
