@@ -153,6 +153,23 @@ def build_workload(config: int, tokens: int, device, rank: int):
     return shapes, weights, xs
 
 
+def run_profile_step(args) -> None:
+    """Two eager forwards of the c1 workload and nothing else: the command profiled by
+    ncu for the per-kernel launch list (the second forward is the one summarised)."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    from int_model_approximation_b200.pipeline import CodebookStack
+
+    tokens = args.profile_tokens
+    _shapes, weights, xs = build_workload(1, tokens, device, 0)
+    stack = CodebookStack(weights)
+    bufs = stack.allocate(tokens)
+    for _ in range(2):
+        stack.forward(xs, bufs)
+        torch.cuda.synchronize()
+    print(json.dumps({"profile_step": "done", "mismatch": int(bufs["mismatch"].item())}))
+
+
 def run_b200(args) -> None:
     world, rank, local = _dist()
     torch.cuda.set_device(local)
@@ -445,10 +462,14 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--reference-rows", type=int, default=64)
+    ap.add_argument("--profile-step", action="store_true", help="two eager forwards only (for ncu)")
+    ap.add_argument("--profile-tokens", type=int, default=TOKENS)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.profile_step:
+        run_profile_step(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)
