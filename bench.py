@@ -203,7 +203,7 @@ def run_b200(args) -> None:
     gemm_graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(gemm_graph, stream=stream):
-            _launch_gemms_only(stack, bufs, TOKENS)
+            stack.forward(xs, bufs, gemm_only=True)
     torch.cuda.synchronize()
 
     def step():
@@ -251,7 +251,7 @@ def run_b200(args) -> None:
         g1.record(stream)
     g1.synchronize()
     gemm_ms_per_step = g0.elapsed_time(g1) / args.steps
-    gemm_launches = len(shapes)
+    gemm_launches = stack.launches_per_forward() - 2
 
     # ---- end to end through the public API: host buffers in, host results out ----
     host_x = [x.cpu().pin_memory() for x in xs]
@@ -316,11 +316,12 @@ def run_b200(args) -> None:
                 "tokens_per_gpu": TOKENS,
                 "exact_int_ops_per_step_per_gpu": flops,
                 "l2": "inputs larger than L2 (about 2.4 GB of weight planes and activations per step)",
-                "launch": "one CUDA graph per step",
+                "launch": "one CUDA graph per step: grouped quantiser, grouped GEMM (40 linears per launch), "
+                          "grouped Freivalds row check",
                 "parallelism": f"replicas x{world} (token batches per rank)",
             },
             "freivalds_mismatch_rows": mismatches,
-            "gpu_launches": len(shapes) * 4 * args.steps,
+            "gpu_launches": stack.launches_per_forward() * args.steps,
             "roofline": {
                 "kernel": "int_gemm_kernel<KARATSUBA3>",
                 "bound": "tensor",
@@ -351,20 +352,6 @@ def run_b200(args) -> None:
     if world > 1:
         del graph, gemm_graph
         torch.distributed.destroy_process_group()
-
-
-def _launch_gemms_only(stack, bufs, tokens):
-    from int_model_approximation_b200 import _native as nat
-
-    lib = nat.lib()
-    stream = nat.stream_of(stack.device)
-    for i, lin in enumerate(stack.linears):
-        planes = bufs["planes"][i]
-        nat.check("ima_int_gemm", lib.ima_int_gemm(
-            planes.planes.data_ptr(), planes.ld, lin.w_planes.planes.data_ptr(), lin.w_planes.ld, tokens, lin.n,
-            lin.k, nat.IMA_SCHEME_KARATSUBA3, bufs["c"][i].data_ptr(), lin.n, bufs["code_scale"][i].data_ptr(),
-            lin.w_code_scale.data_ptr(), nat.ptr(lin.bias), bufs["y"][i].data_ptr(), nat.IMA_DTYPE_BF16, lin.n,
-            stream))
 
 
 def cpu_baseline_sample(shapes, weights, xs, budget_s: float = 15.0) -> dict:

@@ -42,6 +42,9 @@ extern "C" {
 int ima_abi_version(void);                 /* bumped on any signature change */
 const char* ima_status_string(int status); /* static string, never NULL */
 int ima_last_cuda_error(void);             /* cudaError_t of the last failing CUDA call (this thread) */
+/* sizeof of the batch descriptor structs below, in declaration order (quantize, gemm,
+ * freivalds rows), so that foreign-language bindings can check their layouts. */
+int ima_struct_sizes(int64_t* out, int n);
 
 /* Reads (synchronously: waits for the device) and optionally clears the device status
  * word of `device`.  code == IMA_OK when no kernel recorded a failure. */
@@ -61,6 +64,23 @@ int ima_device_status(int device, int* code, int* where, int* detail, int clear)
 int ima_quantize_per_token(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, uint8_t* q_fp8,
                            int64_t ldq, float* scale, int32_t* codebook, int64_t ldc, float* code_scale,
                            int8_t* planes, int64_t ldp, void* stream);
+
+/* The same quantiser for many independent activation matrices in one launch (e.g. every
+ * linear of a model); fields mean what the arguments of ima_quantize_per_token mean. */
+typedef struct ima_quantize_problem {
+    const void* x;
+    int32_t x_dtype;
+    int64_t M, K, ldx;
+    uint8_t* q_fp8;
+    int64_t ldq;
+    float* scale;
+    int32_t* codebook;
+    int64_t ldc;
+    float* code_scale;
+    int8_t* planes;
+    int64_t ldp;
+} ima_quantize_problem;
+int ima_quantize_grouped(const ima_quantize_problem* problems, int count, void* stream);
 
 /* Exact codebook values round(fp8 * 512) of an e4m3 matrix [rows,K] into int32 [rows,K]
  * (row stride ldd).  ref: __main__.py:157-158 _fp8_e4m3_to_int32.  NaN codes give 0,
@@ -104,6 +124,26 @@ int ima_int_gemm(const int8_t* a_planes, int64_t lda, const int8_t* b_planes, in
                  int64_t K, int scheme, int64_t* c, int64_t ldc, const float* x_scale, const float* w_scale,
                  const float* bias, void* y, int y_dtype, int64_t ldy, void* stream);
 
+/* Many independent products in as few launches as possible (one per 40 problems): every
+ * linear of a model in one call.  Fields mean what the arguments of ima_int_gemm mean;
+ * all problems use the same digit scheme. */
+typedef struct ima_gemm_problem {
+    const int8_t* a_planes;
+    int64_t lda;
+    const int8_t* b_planes;
+    int64_t ldb;
+    int64_t M, N, K;
+    int64_t* c;
+    int64_t ldc;
+    const float* x_scale;
+    const float* w_scale;
+    const float* bias;
+    void* y;
+    int32_t y_dtype;
+    int64_t ldy;
+} ima_gemm_problem;
+int ima_int_gemm_grouped(const ima_gemm_problem* problems, int count, int scheme, void* stream);
+
 /* ---- A4: direct Hawkeye replay ---------------------------------------------
  * ref: hawkeye.py:222-275 hawkeye_fp8_sum (kernel hawkeye.py:127-219).
  * Each operand (activations and weights alike) is first staged once with
@@ -126,6 +166,30 @@ int ima_hawkeye_replay(const void* x_operand, const void* w_operand, const float
  * sum_k A[m,k] (sum_n B[k,n] r[n]) != sum_n C[m,n] r[n] (mod 2^64).
  * workspace: device buffer of ima_freivalds_workspace_bytes(K) bytes. */
 int64_t ima_freivalds_workspace_bytes(int64_t K);
+
+/* The weight half of the check, t = codebook(w)^T r (t [K] int64, wrapping), with
+ * w_fp8 [N,K].  It depends only on the weight and the vector, so a verifier that
+ * checks every forward of a linear computes it once and reuses it. */
+int ima_freivalds_weight_vector(const uint8_t* w_fp8, int64_t ldw, const int64_t* r, int64_t N, int64_t K,
+                                int64_t* t, void* stream);
+
+/* The row half for many products in one launch: for each problem, adds to
+ * *mismatch_rows the rows m with A[m,:] . t != C[m,:] . r (mod 2^64).  A is e4m3 codes
+ * (a_kind IMA_FREIVALDS_A_FP8, checked through their codebook values) or int32. */
+#define IMA_FREIVALDS_A_FP8 0
+#define IMA_FREIVALDS_A_INT32 1
+typedef struct ima_freivalds_rows_problem {
+    const void* a;
+    int64_t lda;
+    const int64_t* t;
+    const int64_t* c;
+    int64_t ldc;
+    const int64_t* r;
+    int64_t M, N, K;
+    int32_t a_kind;
+    int32_t* mismatch_rows;
+} ima_freivalds_rows_problem;
+int ima_freivalds_rows_grouped(const ima_freivalds_rows_problem* problems, int count, void* stream);
 /* A = codebook(x_fp8) [M,K], B = codebook(w_fp8)^T with w_fp8 [N,K] (CodebookLinear's operands) */
 int ima_freivalds_fp8(const uint8_t* x_fp8, int64_t ldx, const uint8_t* w_fp8, int64_t ldw, const int64_t* c,
                       int64_t ldc, const int64_t* r, int64_t M, int64_t N, int64_t K, void* workspace,

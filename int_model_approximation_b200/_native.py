@@ -35,9 +35,47 @@ _VP = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int
 
+IMA_FREIVALDS_A_FP8 = 0
+IMA_FREIVALDS_A_INT32 = 1
+
+
+class QuantizeProblem(ctypes.Structure):
+    """ima_quantize_problem"""
+
+    _fields_ = [
+        ("x", _VP), ("x_dtype", ctypes.c_int32), ("M", _I64), ("K", _I64), ("ldx", _I64), ("q_fp8", _VP),
+        ("ldq", _I64), ("scale", _VP), ("codebook", _VP), ("ldc", _I64), ("code_scale", _VP), ("planes", _VP),
+        ("ldp", _I64),
+    ]
+
+
+class GemmProblem(ctypes.Structure):
+    """ima_gemm_problem"""
+
+    _fields_ = [
+        ("a_planes", _VP), ("lda", _I64), ("b_planes", _VP), ("ldb", _I64), ("M", _I64), ("N", _I64), ("K", _I64),
+        ("c", _VP), ("ldc", _I64), ("x_scale", _VP), ("w_scale", _VP), ("bias", _VP), ("y", _VP),
+        ("y_dtype", ctypes.c_int32), ("ldy", _I64),
+    ]
+
+
+class FreivaldsRowsProblem(ctypes.Structure):
+    """ima_freivalds_rows_problem"""
+
+    _fields_ = [
+        ("a", _VP), ("lda", _I64), ("t", _VP), ("c", _VP), ("ldc", _I64), ("r", _VP), ("M", _I64), ("N", _I64),
+        ("K", _I64), ("a_kind", ctypes.c_int32), ("mismatch_rows", _VP),
+    ]
+
+
 # name -> (restype, argtypes); mirrors include/ima_b200.h
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ima_abi_version": (_I32, []),
+    "ima_struct_sizes": (_I32, [_VP, _I32]),
+    "ima_quantize_grouped": (_I32, [_VP, _I32, _VP]),
+    "ima_int_gemm_grouped": (_I32, [_VP, _I32, _I32, _VP]),
+    "ima_freivalds_weight_vector": (_I32, [_VP, _I64, _VP, _I64, _I64, _VP, _VP]),
+    "ima_freivalds_rows_grouped": (_I32, [_VP, _I32, _VP]),
     "ima_status_string": (ctypes.c_char_p, [_I32]),
     "ima_last_cuda_error": (_I32, []),
     "ima_device_status": (_I32, [_I32, _VP, _VP, _VP, _I32]),

@@ -5,51 +5,66 @@
 // single corrupted entry C[m,n] + d is rejected whenever d * r[n] != 0 mod 2^64).
 //
 // Two bandwidth-bound GEMV passes:
-//   pass 1  t = B r          (reads B once: N*K codes)
-//   pass 2  per row m: A[m,:] . t  vs  C[m,:] . r   (reads A and C once: M*K + 8*M*N bytes)
+//   weight pass  t = B r          (reads B once: N*K codes).  B and r are fixed per
+//                linear, so a caller that checks many products of the same weight
+//                computes t once (ima_freivalds_weight_vector) and reuses it.
+//   row pass     per row m: A[m,:] . t  vs  C[m,:] . r  (reads A and C once: M*K + 8*M*N
+//                bytes); one warp per row, many products per launch.
 // All arithmetic is uint64 (wrapping), identical to the CPU oracle.
 #include "ima_common.cuh"
 
 namespace {
 
 constexpr int FV_THREADS = 256;
-constexpr int FV_COLS_PER_THREAD = 16;   // fp8 pass 1: one 16-byte load per row per thread
-constexpr int FV_ROWS_PER_BLOCK = 64;    // fp8 pass 1: rows (n) summed by one block before the atomic
+constexpr int FV_WCOLS = 16;    // weight pass: 16 consecutive k per thread (one 16-byte load per row)
+constexpr int FV_WROWS = 32;    // weight pass: rows n summed per thread before the atomic
 
-// Pass 1 for fp8 weights w [N,K]: t[k] += sum_{n in block rows} code(w[n,k]) * r[n].
-__global__ void __launch_bounds__(FV_THREADS) fv_br_fp8_kernel(const uint8_t* __restrict__ w, int64_t ldw,
-                                                              const int64_t* __restrict__ r, int64_t N, int64_t K,
-                                                              unsigned long long* __restrict__ t) {
-    int64_t k0 = ((int64_t)blockIdx.x * FV_THREADS + threadIdx.x) * FV_COLS_PER_THREAD;
-    int64_t n0 = (int64_t)blockIdx.y * FV_ROWS_PER_BLOCK;
-    if (k0 >= K) return;
-    uint64_t acc[FV_COLS_PER_THREAD];
+// Weight pass for fp8 weights w [N,K]: t[k] += sum_{n in chunk} code(w[n,k]) * r[n].
+__global__ void __launch_bounds__(FV_THREADS) fv_weight_fp8_kernel(const uint8_t* __restrict__ w, int64_t ldw,
+                                                                  const int64_t* __restrict__ r, int64_t N, int64_t K,
+                                                                  unsigned long long* __restrict__ t) {
+    const int64_t k_groups = (K + FV_WCOLS - 1) / FV_WCOLS;
+    const int64_t idx = (int64_t)blockIdx.x * FV_THREADS + threadIdx.x;
+    const int64_t kg = idx % k_groups;
+    const int64_t n0 = (idx / k_groups) * FV_WROWS;
+    if (n0 >= N) return;
+    const int64_t k0 = kg * FV_WCOLS;
+    uint64_t acc[FV_WCOLS];
 #pragma unroll
-    for (int j = 0; j < FV_COLS_PER_THREAD; ++j) acc[j] = 0;
-    int64_t n1 = n0 + FV_ROWS_PER_BLOCK < N ? n0 + FV_ROWS_PER_BLOCK : N;
-    bool vec = (k0 + FV_COLS_PER_THREAD <= K) && ((ldw & 15) == 0) && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);
+    for (int j = 0; j < FV_WCOLS; ++j) acc[j] = 0;
+    const int64_t n1 = n0 + FV_WROWS < N ? n0 + FV_WROWS : N;
+    const bool vec = (k0 + FV_WCOLS <= K) && ((ldw & 15) == 0) && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);
     for (int64_t n = n0; n < n1; ++n) {
-        uint64_t rn = (uint64_t)r[n];
-        uint8_t b[FV_COLS_PER_THREAD];
+        const uint64_t rn = (uint64_t)__ldg(r + n);
+        uint32_t wd[4];
         if (vec) {
             uint4 v = __ldg(reinterpret_cast<const uint4*>(w + n * ldw + k0));
-            memcpy(b, &v, 16);
+            wd[0] = v.x; wd[1] = v.y; wd[2] = v.z; wd[3] = v.w;
         } else {
 #pragma unroll
-            for (int j = 0; j < FV_COLS_PER_THREAD; ++j) b[j] = (k0 + j < K) ? w[n * ldw + k0 + j] : 0;
+            for (int q = 0; q < 4; ++q) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    int64_t k = k0 + q * 4 + b;
+                    if (k < K) word |= (uint32_t)w[n * ldw + k] << (8 * b);
+                }
+                wd[q] = word;
+            }
         }
 #pragma unroll
-        for (int j = 0; j < FV_COLS_PER_THREAD; ++j) acc[j] += (uint64_t)(int64_t)ima_e4m3_codebook(b[j]) * rn;
+        for (int j = 0; j < FV_WCOLS; ++j)
+            acc[j] += (uint64_t)(int64_t)ima_e4m3_codebook((wd[j >> 2] >> (8 * (j & 3))) & 0xFFu) * rn;
     }
 #pragma unroll
-    for (int j = 0; j < FV_COLS_PER_THREAD; ++j)
+    for (int j = 0; j < FV_WCOLS; ++j)
         if (k0 + j < K) atomicAdd(t + k0 + j, (unsigned long long)acc[j]);
 }
 
-// Pass 1 for int32 b [K,N] (row-major, the reference's weight_t): one warp per row k.
-__global__ void __launch_bounds__(FV_THREADS) fv_br_i32_kernel(const int32_t* __restrict__ b, int64_t ldb,
-                                                              const int64_t* __restrict__ r, int64_t N, int64_t K,
-                                                              unsigned long long* __restrict__ t) {
+// Weight pass for int32 b [K,N] (row-major, the reference's weight_t): one warp per row k.
+__global__ void __launch_bounds__(FV_THREADS) fv_weight_i32_kernel(const int32_t* __restrict__ b, int64_t ldb,
+                                                                  const int64_t* __restrict__ r, int64_t N, int64_t K,
+                                                                  unsigned long long* __restrict__ t) {
     int64_t k = (int64_t)blockIdx.x * (FV_THREADS / 32) + (threadIdx.x >> 5);
     int lane = threadIdx.x & 31;
     if (k >= K) return;
@@ -59,53 +74,99 @@ __global__ void __launch_bounds__(FV_THREADS) fv_br_i32_kernel(const int32_t* __
     if (lane == 0) t[k] = acc;
 }
 
-IMA_DEVINL uint64_t block_sum_u64(uint64_t v, uint64_t* s_red) {
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) s_red[warp] = v;
-    __syncthreads();
-    uint64_t s = 0;
-    if (threadIdx.x == 0)
-        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += s_red[i];
-    __syncthreads();
-    return s;   // valid in thread 0 only
-}
+}  // namespace
 
-// Pass 2: one block per row m.  A is fp8 codes (kind 0) or int32 (kind 1).
-template <int KIND>
-__global__ void __launch_bounds__(FV_THREADS) fv_rows_kernel(const void* __restrict__ a, int64_t lda,
-                                                            const unsigned long long* __restrict__ t,
-                                                            const int64_t* __restrict__ c, int64_t ldc,
-                                                            const int64_t* __restrict__ r, int64_t M, int64_t N,
-                                                            int64_t K, int32_t* __restrict__ mismatch_rows) {
-    __shared__ uint64_t s_red[FV_THREADS / 32];
-    for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
-        uint64_t lhs = 0, rhs = 0;
-        for (int64_t k = threadIdx.x; k < K; k += FV_THREADS) {
-            int64_t av;
-            if (KIND == 0) av = ima_e4m3_codebook(reinterpret_cast<const uint8_t*>(a)[m * lda + k]);
-            else av = reinterpret_cast<const int32_t*>(a)[m * lda + k];
-            lhs += (uint64_t)av * (uint64_t)t[k];
+// One product of a row-pass batch.
+struct FvRowProblem {
+    const void* a;           // activations: fp8 codes (a_kind 0) or int32 (a_kind 1), [M, K] row stride lda
+    const unsigned long long* t;   // [K] = B r
+    const int64_t* c;        // [M, N] row stride ldc
+    const int64_t* r;        // [N]
+    int32_t* mismatch;       // device counter
+    int64_t lda, ldc, M, N, K;
+    int64_t row_start;       // first global row of this product in the batch
+    int32_t a_kind, pad;
+};
+
+constexpr int FV_MAXP = 192;
+struct FvRowBatch {
+    FvRowProblem p[FV_MAXP];
+    int32_t n;
+    int64_t total_rows;
+};
+
+namespace {
+
+// Row pass: one warp per (product, row); products located by binary search on row_start.
+__global__ void __launch_bounds__(FV_THREADS) fv_rows_kernel(const __grid_constant__ FvRowBatch batch) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps_total = (int64_t)gridDim.x * (FV_THREADS / 32);
+    for (int64_t g = (int64_t)blockIdx.x * (FV_THREADS / 32) + (threadIdx.x >> 5); g < batch.total_rows;
+         g += warps_total) {
+        int lo = 0, hi = batch.n - 1;
+        while (lo < hi) {
+            int mid = (lo + hi + 1) >> 1;
+            if (batch.p[mid].row_start <= g) lo = mid; else hi = mid - 1;
         }
-        const int64_t* crow = c + m * ldc;
-        bool vec = ((reinterpret_cast<uintptr_t>(crow) & 15) == 0) && ((reinterpret_cast<uintptr_t>(r) & 15) == 0);
-        if (vec) {
-            int64_t n2 = N / 2;
-            for (int64_t i = threadIdx.x; i < n2; i += FV_THREADS) {
-                longlong2 cv = __ldcs(reinterpret_cast<const longlong2*>(crow) + i);   // streamed: read once
-                longlong2 rv = __ldg(reinterpret_cast<const longlong2*>(r) + i);
+        const FvRowProblem& P = batch.p[lo];
+        const int64_t m = g - P.row_start;
+        uint64_t lhs = 0, rhs = 0;
+        if (P.a_kind == 0) {
+            const uint8_t* arow = reinterpret_cast<const uint8_t*>(P.a) + m * P.lda;
+            const bool vec = ((reinterpret_cast<uintptr_t>(arow) & 3) == 0);
+            if (vec) {
+                const int64_t k4 = P.K / 4;
+                for (int64_t i = lane; i < k4; i += 32) {
+                    uint32_t wd = __ldg(reinterpret_cast<const uint32_t*>(arow) + i);
+#pragma unroll
+                    for (int b = 0; b < 4; ++b)
+                        lhs += (uint64_t)(int64_t)ima_e4m3_codebook((wd >> (8 * b)) & 0xFFu) * (uint64_t)P.t[4 * i + b];
+                }
+                for (int64_t k = 4 * k4 + lane; k < P.K; k += 32)
+                    lhs += (uint64_t)(int64_t)ima_e4m3_codebook(arow[k]) * (uint64_t)P.t[k];
+            } else {
+                for (int64_t k = lane; k < P.K; k += 32)
+                    lhs += (uint64_t)(int64_t)ima_e4m3_codebook(arow[k]) * (uint64_t)P.t[k];
+            }
+        } else {
+            const int32_t* arow = reinterpret_cast<const int32_t*>(P.a) + m * P.lda;
+            for (int64_t k = lane; k < P.K; k += 32) lhs += (uint64_t)(int64_t)arow[k] * (uint64_t)P.t[k];
+        }
+        const int64_t* crow = P.c + m * P.ldc;
+        const bool cvec = ((reinterpret_cast<uintptr_t>(crow) & 15) == 0) && ((reinterpret_cast<uintptr_t>(P.r) & 15) == 0);
+        if (cvec) {
+            const int64_t n2 = P.N / 2;
+            for (int64_t i = lane; i < n2; i += 32) {
+                longlong2 cv = __ldcs(reinterpret_cast<const longlong2*>(crow) + i);   // read once: stream
+                longlong2 rv = __ldg(reinterpret_cast<const longlong2*>(P.r) + i);
                 rhs += (uint64_t)cv.x * (uint64_t)rv.x + (uint64_t)cv.y * (uint64_t)rv.y;
             }
-            if (threadIdx.x == 0 && (N & 1)) rhs += (uint64_t)crow[N - 1] * (uint64_t)r[N - 1];
+            if (lane == 0 && (P.N & 1)) rhs += (uint64_t)crow[P.N - 1] * (uint64_t)P.r[P.N - 1];
         } else {
-            for (int64_t n = threadIdx.x; n < N; n += FV_THREADS) rhs += (uint64_t)crow[n] * (uint64_t)r[n];
+            for (int64_t n = lane; n < P.N; n += 32) rhs += (uint64_t)crow[n] * (uint64_t)P.r[n];
         }
-        uint64_t d = block_sum_u64(lhs - rhs, s_red);
-        if (threadIdx.x == 0 && d != 0) atomicAdd(mismatch_rows, 1);
+        uint64_t d = lhs - rhs;   // the row passes iff the lane partial differences sum to 0 (mod 2^64)
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
+        if (lane == 0 && d != 0) atomicAdd(P.mismatch, 1);
     }
 }
 
-inline unsigned rows_grid(int64_t M) { return (unsigned)(M < 148 * 16 ? M : 148 * 16); }
+int launch_rows(const FvRowBatch& b, cudaStream_t s) {
+    if (b.total_rows == 0) return IMA_OK;
+    int64_t blocks = (b.total_rows + (FV_THREADS / 32) - 1) / (FV_THREADS / 32);
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    fv_rows_kernel<<<(unsigned)blocks, FV_THREADS, 0, s>>>(b);
+    return IMA_LAUNCH_STATUS();
+}
+
+int weight_vector_fp8(const uint8_t* w, int64_t ldw, const int64_t* r, int64_t N, int64_t K,
+                      unsigned long long* t, cudaStream_t s) {
+    int rc = ima_note_cuda(cudaMemsetAsync(t, 0, (size_t)(K > 0 ? K : 1) * 8, s));
+    if (rc != IMA_OK || K == 0 || N == 0) return rc;
+    int64_t units = ((K + FV_WCOLS - 1) / FV_WCOLS) * ((N + FV_WROWS - 1) / FV_WROWS);
+    fv_weight_fp8_kernel<<<(unsigned)((units + FV_THREADS - 1) / FV_THREADS), FV_THREADS, 0, s>>>(w, ldw, r, N, K, t);
+    return IMA_LAUNCH_STATUS();
+}
 
 }  // namespace
 
@@ -113,26 +174,50 @@ extern "C" {
 
 int64_t ima_freivalds_workspace_bytes(int64_t K) { return (K > 0 ? K : 1) * 8; }
 
+int ima_freivalds_weight_vector(const uint8_t* w_fp8, int64_t ldw, const int64_t* r, int64_t N, int64_t K,
+                                int64_t* t, void* stream) {
+    if (!w_fp8 || !r || !t || N < 0 || K < 0 || ldw < K) return IMA_ERR_INVALID_ARGUMENT;
+    return weight_vector_fp8(w_fp8, ldw, r, N, K, reinterpret_cast<unsigned long long*>(t), (cudaStream_t)stream);
+}
+
+int ima_freivalds_rows_grouped(const ima_freivalds_rows_problem* problems, int count, void* stream) {
+    if (count < 0 || (count > 0 && !problems)) return IMA_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < count; ++i) {
+        const ima_freivalds_rows_problem& q = problems[i];
+        if (!q.a || !q.t || !q.c || !q.r || !q.mismatch_rows) return IMA_ERR_INVALID_ARGUMENT;
+        if (q.M < 0 || q.N < 0 || q.K < 0 || q.lda < q.K || q.ldc < q.N) return IMA_ERR_INVALID_ARGUMENT;
+        if (q.a_kind != IMA_FREIVALDS_A_FP8 && q.a_kind != IMA_FREIVALDS_A_INT32) return IMA_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    FvRowBatch b;
+    memset(&b, 0, sizeof(b));
+    for (int i = 0; i < count; ++i) {
+        const ima_freivalds_rows_problem& q = problems[i];
+        FvRowProblem& P = b.p[b.n];
+        P.a = q.a; P.t = reinterpret_cast<const unsigned long long*>(q.t); P.c = q.c; P.r = q.r;
+        P.mismatch = q.mismatch_rows; P.lda = q.lda; P.ldc = q.ldc; P.M = q.M; P.N = q.N; P.K = q.K;
+        P.a_kind = q.a_kind; P.row_start = b.total_rows;
+        b.total_rows += q.M;
+        if (++b.n == FV_MAXP) {
+            int rc = launch_rows(b, s);
+            if (rc != IMA_OK) return rc;
+            memset(&b, 0, sizeof(b));
+        }
+    }
+    return b.n ? launch_rows(b, s) : IMA_OK;
+}
+
 int ima_freivalds_fp8(const uint8_t* x_fp8, int64_t ldx, const uint8_t* w_fp8, int64_t ldw, const int64_t* c,
                       int64_t ldc, const int64_t* r, int64_t M, int64_t N, int64_t K, void* workspace,
                       int32_t* mismatch_rows, void* stream) {
     if (!x_fp8 || !w_fp8 || !c || !r || !workspace || !mismatch_rows) return IMA_ERR_INVALID_ARGUMENT;
     if (M < 0 || N < 0 || K < 0 || ldx < K || ldw < K || ldc < N) return IMA_ERR_INVALID_ARGUMENT;
     if (M == 0) return IMA_OK;
-    cudaStream_t s = (cudaStream_t)stream;
-    unsigned long long* t = reinterpret_cast<unsigned long long*>(workspace);
-    int rc = ima_note_cuda(cudaMemsetAsync(t, 0, (size_t)(K > 0 ? K : 1) * 8, s));
+    int rc = ima_freivalds_weight_vector(w_fp8, ldw, r, N, K, reinterpret_cast<int64_t*>(workspace), stream);
     if (rc != IMA_OK) return rc;
-    if (K > 0 && N > 0) {
-        dim3 g1((unsigned)((K + FV_THREADS * FV_COLS_PER_THREAD - 1) / (FV_THREADS * FV_COLS_PER_THREAD)),
-                (unsigned)((N + FV_ROWS_PER_BLOCK - 1) / FV_ROWS_PER_BLOCK));
-        if (g1.y > 65535u) return IMA_ERR_UNSUPPORTED;
-        fv_br_fp8_kernel<<<g1, FV_THREADS, 0, s>>>(w_fp8, ldw, r, N, K, t);
-        rc = IMA_LAUNCH_STATUS();
-        if (rc != IMA_OK) return rc;
-    }
-    fv_rows_kernel<0><<<rows_grid(M), FV_THREADS, 0, s>>>(x_fp8, ldx, t, c, ldc, r, M, N, K, mismatch_rows);
-    return IMA_LAUNCH_STATUS();
+    ima_freivalds_rows_problem q = {x_fp8, ldx, reinterpret_cast<const int64_t*>(workspace), c, ldc, r,
+                                    M, N, K, IMA_FREIVALDS_A_FP8, mismatch_rows};
+    return ima_freivalds_rows_grouped(&q, 1, stream);
 }
 
 int ima_freivalds_i32(const int32_t* a, int64_t lda, const int32_t* b, int64_t ldb, const int64_t* c, int64_t ldc,
@@ -143,16 +228,15 @@ int ima_freivalds_i32(const int32_t* a, int64_t lda, const int32_t* b, int64_t l
     if (M == 0) return IMA_OK;
     cudaStream_t s = (cudaStream_t)stream;
     unsigned long long* t = reinterpret_cast<unsigned long long*>(workspace);
-    int rc = ima_note_cuda(cudaMemsetAsync(t, 0, (size_t)(K > 0 ? K : 1) * 8, s));
-    if (rc != IMA_OK) return rc;
     if (K > 0) {
         unsigned g1 = (unsigned)((K + FV_THREADS / 32 - 1) / (FV_THREADS / 32));
-        fv_br_i32_kernel<<<g1, FV_THREADS, 0, s>>>(b, ldb, r, N, K, t);
-        rc = IMA_LAUNCH_STATUS();
+        fv_weight_i32_kernel<<<g1, FV_THREADS, 0, s>>>(b, ldb, r, N, K, t);
+        int rc = IMA_LAUNCH_STATUS();
         if (rc != IMA_OK) return rc;
     }
-    fv_rows_kernel<1><<<rows_grid(M), FV_THREADS, 0, s>>>(a, lda, t, c, ldc, r, M, N, K, mismatch_rows);
-    return IMA_LAUNCH_STATUS();
+    ima_freivalds_rows_problem q = {a, lda, reinterpret_cast<const int64_t*>(workspace), c, ldc, r,
+                                    M, N, K, IMA_FREIVALDS_A_INT32, mismatch_rows};
+    return ima_freivalds_rows_grouped(&q, 1, stream);
 }
 
 }  // extern "C"

@@ -40,17 +40,56 @@ IMA_DEVINL void digits5(int32_t v, int32_t d[5]) {
     d[4] = (int32_t)w;  // |w| <= 8 for any int32
 }
 
-// One CTA per row (grid-stride).  Pass 1: NaN-propagating amax.  Pass 2: quantise
-// four consecutive columns per thread-iteration so each plane store is one 32-bit word.
-__global__ void __launch_bounds__(256) quantize_rows_kernel(const void* __restrict__ x, int dtype, int64_t M,
-                                                            int64_t K, int64_t ldx, uint8_t* __restrict__ q,
-                                                            int64_t ldq, float* __restrict__ scale_out,
-                                                            int32_t* __restrict__ codebook, int64_t ldc,
-                                                            float* __restrict__ code_scale,
-                                                            int8_t* __restrict__ planes, int64_t ldp) {
+}  // namespace
+
+// One quantisation problem of a batch (a kernel parameter; no device-side descriptor memory).
+struct QuantProblem {
+    const void* x;
+    int64_t ldx;
+    int64_t M, K;
+    uint8_t* q;
+    int64_t ldq;
+    float* scale;
+    float* code_scale;
+    int32_t* codebook;
+    int64_t ldc;
+    int8_t* planes;
+    int64_t ldp;
+    int64_t row_start;
+    int32_t dtype, pad;
+};
+
+constexpr int QZ_MAXP = 192;
+struct QuantBatch {
+    QuantProblem p[QZ_MAXP];
+    int32_t n;
+    int64_t total_rows;
+};
+
+namespace {
+
+// One CTA per (problem, row), grid-stride over all rows of the batch.  Pass 1:
+// NaN-propagating amax.  Pass 2: quantise four consecutive columns per thread-iteration
+// so each plane store is one 32-bit word.
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constant__ QuantBatch batch) {
     __shared__ float s_red[32];
     __shared__ int s_nan[32];
-    for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
+    for (int64_t g = blockIdx.x; g < batch.total_rows; g += gridDim.x) {
+        int lo = 0, hi = batch.n - 1;
+        while (lo < hi) {
+            int mid = (lo + hi + 1) >> 1;
+            if (batch.p[mid].row_start <= g) lo = mid; else hi = mid - 1;
+        }
+        const QuantProblem& P = batch.p[lo];
+        const int64_t m = g - P.row_start;
+        const void* x = P.x;
+        const int dtype = P.dtype;
+        const int64_t M = P.M, K = P.K, ldx = P.ldx, ldq = P.ldq, ldc = P.ldc, ldp = P.ldp;
+        uint8_t* q = P.q;
+        float* scale_out = P.scale;
+        float* code_scale = P.code_scale;
+        int32_t* codebook = P.codebook;
+        int8_t* planes = P.planes;
         float amax = 0.0f;
         int has_nan = 0;
         for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
@@ -198,19 +237,52 @@ int ima_scheme_planes(int scheme) {
     return scheme == IMA_SCHEME_KARATSUBA3 ? 6 : (scheme == IMA_SCHEME_DIGITS5 ? 5 : 0);
 }
 
+static int check_quant_problem(const ima_quantize_problem& q) {
+    if (!q.x || !q.q_fp8 || !q.scale || q.M < 0 || q.K < 0 || q.ldx < q.K || q.ldq < q.K) return IMA_ERR_INVALID_ARGUMENT;
+    if (q.x_dtype != IMA_DTYPE_F32 && q.x_dtype != IMA_DTYPE_BF16 && q.x_dtype != IMA_DTYPE_F16)
+        return IMA_ERR_INVALID_ARGUMENT;
+    if (q.codebook && q.ldc < q.K) return IMA_ERR_INVALID_ARGUMENT;
+    if (q.planes && (q.ldp < q.K || q.ldp % 16 != 0 || (reinterpret_cast<uintptr_t>(q.planes) & 15)))
+        return IMA_ERR_INVALID_ARGUMENT;
+    return IMA_OK;
+}
+
+static int launch_quant(const QuantBatch& b, cudaStream_t s) {
+    if (b.total_rows == 0) return IMA_OK;
+    int64_t grid = b.total_rows < 148 * 64 ? b.total_rows : 148 * 64;
+    quantize_rows_kernel<<<(unsigned)grid, 256, 0, s>>>(b);
+    return IMA_LAUNCH_STATUS();
+}
+
+int ima_quantize_grouped(const ima_quantize_problem* problems, int count, void* stream) {
+    if (count < 0 || (count > 0 && !problems)) return IMA_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < count; ++i) {
+        int rc = check_quant_problem(problems[i]);
+        if (rc != IMA_OK) return rc;
+    }
+    QuantBatch b;
+    memset(&b, 0, sizeof(b));
+    for (int i = 0; i < count; ++i) {
+        const ima_quantize_problem& q = problems[i];
+        QuantProblem& P = b.p[b.n];
+        P.x = q.x; P.ldx = q.ldx; P.M = q.M; P.K = q.K; P.q = q.q_fp8; P.ldq = q.ldq; P.scale = q.scale;
+        P.code_scale = q.code_scale; P.codebook = q.codebook; P.ldc = q.ldc; P.planes = q.planes; P.ldp = q.ldp;
+        P.dtype = q.x_dtype; P.row_start = b.total_rows;
+        b.total_rows += q.M;
+        if (++b.n == QZ_MAXP) {
+            int rc = launch_quant(b, (cudaStream_t)stream);
+            if (rc != IMA_OK) return rc;
+            memset(&b, 0, sizeof(b));
+        }
+    }
+    return b.n ? launch_quant(b, (cudaStream_t)stream) : IMA_OK;
+}
+
 int ima_quantize_per_token(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, uint8_t* q_fp8,
                            int64_t ldq, float* scale, int32_t* codebook, int64_t ldc, float* code_scale,
                            int8_t* planes, int64_t ldp, void* stream) {
-    if (!x || !q_fp8 || !scale || M < 0 || K < 0 || ldx < K || ldq < K) return IMA_ERR_INVALID_ARGUMENT;
-    if (x_dtype != IMA_DTYPE_F32 && x_dtype != IMA_DTYPE_BF16 && x_dtype != IMA_DTYPE_F16)
-        return IMA_ERR_INVALID_ARGUMENT;
-    if (codebook && ldc < K) return IMA_ERR_INVALID_ARGUMENT;
-    if (planes && (ldp < K || ldp % 16 != 0 || (reinterpret_cast<uintptr_t>(planes) & 15))) return IMA_ERR_INVALID_ARGUMENT;
-    if (M == 0) return IMA_OK;
-    unsigned grid = (unsigned)(M < 65535 * 8 ? M : 65535 * 8);
-    quantize_rows_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, x_dtype, M, K, ldx, q_fp8, ldq, scale, codebook,
-                                                                 ldc, code_scale, planes, ldp);
-    return IMA_LAUNCH_STATUS();
+    ima_quantize_problem q = {x, x_dtype, M, K, ldx, q_fp8, ldq, scale, codebook, ldc, code_scale, planes, ldp};
+    return ima_quantize_grouped(&q, 1, stream);
 }
 
 int ima_codebook_from_fp8(const uint8_t* src, int64_t rows, int64_t K, int64_t ld, int32_t* dst, int64_t ldd,

@@ -29,6 +29,14 @@ const char* ima_status_string(int status) {
 
 int ima_last_cuda_error(void) { return g_last_cuda_error; }
 
+int ima_struct_sizes(int64_t* out, int n) {
+    if (!out || n < 3) return IMA_ERR_INVALID_ARGUMENT;
+    out[0] = (int64_t)sizeof(ima_quantize_problem);
+    out[1] = (int64_t)sizeof(ima_gemm_problem);
+    out[2] = (int64_t)sizeof(ima_freivalds_rows_problem);
+    return IMA_OK;
+}
+
 int ima_device_status(int device, int* code, int* where, int* detail, int clear) {
     int prev = 0;
     if (cudaGetDevice(&prev) != cudaSuccess) return ima_note_cuda(cudaGetLastError());

@@ -24,6 +24,22 @@ def freivalds_vector(n: int, seed: int, device: torch.device | str = "cpu") -> t
     return r.to(device)
 
 
+def weight_vector(w_fp8: torch.Tensor, r: torch.Tensor) -> torch.Tensor:
+    """t = codebook(w)^T r (int64 [K], wrapping): the weight half of the check, fixed for
+    a given weight and vector, so it is computed once per linear."""
+    w = w_fp8.contiguous().view(torch.uint8)
+    n, k = w.shape
+    if r.dtype != torch.int64 or r.numel() != n:
+        raise RuntimeError("Freivalds vector must be int64 with one entry per weight row")
+    r = r.reshape(-1).contiguous()
+    nat.require_device(w.device, ("vector", r))
+    t = torch.empty((max(k, 1),), dtype=torch.int64, device=w.device)
+    with torch.cuda.device(w.device):
+        nat.call("ima_freivalds_weight_vector", w.data_ptr(), k, r.data_ptr(), n, k, t.data_ptr(),
+                 nat.stream_of(w.device))
+    return t[:k]
+
+
 def _workspace(k: int, device: torch.device) -> torch.Tensor:
     nbytes = int(nat.lib().ima_freivalds_workspace_bytes(k))
     return torch.empty((nbytes // 8,), dtype=torch.int64, device=device)

@@ -1,25 +1,28 @@
 """A model's worth of student linears prepared for repeated forwards.
 
 `CodebookStack` holds every linear of a model in the codebook student form
-(weights prepacked once into digit planes, a Freivalds vector per linear) and runs
-one forward of all of them -- per-token quantisation, the exact int64 GEMM with the
-fused rescale/bias/bf16 epilogue, and the Freivalds check of each int64 product --
-entirely on the device, with no host synchronisation.  The sequence of launches can
-be captured once into a CUDA graph and replayed.
+(weights prepacked once into digit planes; per linear a Freivalds vector r and the
+weight half of the check t = codebook(W)^T r, both fixed) and runs one forward of all
+of them -- per-token quantisation, the exact int64 GEMM with the fused
+rescale/bias/bf16 epilogue, and the Freivalds row check of every int64 product -- as
+three grouped launches kinds (one quantiser launch, one GEMM launch per 40 linears, one
+Freivalds launch), entirely on the device and without host synchronisation.  The
+launch sequence can be captured once into a CUDA graph and replayed.
 
 `HawkeyeStack` does the same for the direct Hawkeye replay student.
 """
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
 
 from . import _native as nat
-from .codebook import DigitPlanes, codebook_planes_from_fp8, int_gemm
-from .freivalds import freivalds_vector
-from .hawkeye import HawkeyeOperand, hawkeye_replay
+from .codebook import DigitPlanes, codebook_planes_from_fp8
+from .freivalds import freivalds_vector, weight_vector
+from .hawkeye import HawkeyeOperand
 
 
 @dataclass
@@ -31,13 +34,17 @@ class PreparedLinear:
     w_code_scale: torch.Tensor   # [N] fp32 = weight_scale / 512
     bias: torch.Tensor | None    # [N] fp32
     r: torch.Tensor              # [N] int64 Freivalds vector
+    t: torch.Tensor              # [K] int64 = codebook(w)^T r
 
 
 class CodebookStack:
+    GEMM_BATCH = 40   # problems per GEMM launch (kernel-parameter budget of the C side)
+
     def __init__(self, weights: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]], *, seed: int = 0):
         self.linears: list[PreparedLinear] = []
         for i, (w, ws, bias) in enumerate(weights):
             planes, _ = codebook_planes_from_fp8(w)
+            r = freivalds_vector(int(w.shape[0]), seed * 100_003 + i + 7, device=w.device)
             self.linears.append(
                 PreparedLinear(
                     n=int(w.shape[0]),
@@ -46,7 +53,8 @@ class CodebookStack:
                     w_planes=planes,
                     w_code_scale=(ws.reshape(-1).to(torch.float32) / 512.0).contiguous(),
                     bias=None if bias is None else bias.reshape(-1).to(torch.float32).contiguous(),
-                    r=freivalds_vector(int(w.shape[0]), seed * 100_003 + i + 7, device=w.device),
+                    r=r,
+                    t=weight_vector(w, r),
                 )
             )
         self.device = weights[0][0].device
@@ -54,48 +62,70 @@ class CodebookStack:
     def allocate(self, tokens: int) -> dict:
         """Per-forward buffers for `tokens` rows (reused by every forward / graph replay)."""
         dev = self.device
-        bufs = dict(q=[], scale=[], planes=[], c=[], y=[], ws=[])
+        bufs = dict(q=[], scale=[], code_scale=[], planes=[], c=[], y=[])
         for lin in self.linears:
             bufs["q"].append(torch.empty((tokens, lin.k), dtype=torch.uint8, device=dev))
             bufs["scale"].append(torch.empty((tokens,), dtype=torch.float32, device=dev))
+            bufs["code_scale"].append(torch.empty((tokens,), dtype=torch.float32, device=dev))
             bufs["planes"].append(DigitPlanes.empty(tokens, lin.k, nat.IMA_SCHEME_KARATSUBA3, dev))
             bufs["c"].append(torch.empty((tokens, lin.n), dtype=torch.int64, device=dev))
             bufs["y"].append(torch.empty((tokens, lin.n), dtype=torch.bfloat16, device=dev))
-            bufs["ws"].append(torch.empty((int(nat.lib().ima_freivalds_workspace_bytes(lin.k)) // 8,),
-                                          dtype=torch.int64, device=dev))
         bufs["mismatch"] = torch.zeros((1,), dtype=torch.int32, device=dev)
-        bufs["code_scale"] = [torch.empty((tokens,), dtype=torch.float32, device=dev) for _ in self.linears]
+        bufs["tokens"] = tokens
         return bufs
 
-    def forward(self, xs: list[torch.Tensor], bufs: dict, *, check: bool = True) -> None:
+    def _descriptors(self, xs: list[torch.Tensor], bufs: dict) -> tuple:
+        n = len(self.linears)
+        quant = (nat.QuantizeProblem * n)()
+        gemm = (nat.GemmProblem * n)()
+        rows = (nat.FreivaldsRowsProblem * n)()
+        for i, lin in enumerate(self.linears):
+            x = xs[i]
+            m = int(x.shape[0])
+            planes = bufs["planes"][i]
+            q = quant[i]
+            q.x, q.x_dtype, q.M, q.K, q.ldx = x.data_ptr(), nat.dtype_code(x.dtype), m, lin.k, x.stride(0)
+            q.q_fp8, q.ldq, q.scale = bufs["q"][i].data_ptr(), lin.k, bufs["scale"][i].data_ptr()
+            q.codebook, q.ldc, q.code_scale = None, lin.k, bufs["code_scale"][i].data_ptr()
+            q.planes, q.ldp = planes.planes.data_ptr(), planes.ld
+            g = gemm[i]
+            g.a_planes, g.lda, g.b_planes, g.ldb = planes.planes.data_ptr(), planes.ld, \
+                lin.w_planes.planes.data_ptr(), lin.w_planes.ld
+            g.M, g.N, g.K = m, lin.n, lin.k
+            g.c, g.ldc = bufs["c"][i].data_ptr(), lin.n
+            g.x_scale, g.w_scale = bufs["code_scale"][i].data_ptr(), lin.w_code_scale.data_ptr()
+            g.bias = nat.ptr(lin.bias)
+            g.y, g.y_dtype, g.ldy = bufs["y"][i].data_ptr(), nat.IMA_DTYPE_BF16, lin.n
+            f = rows[i]
+            f.a, f.lda, f.t = bufs["q"][i].data_ptr(), lin.k, lin.t.data_ptr()
+            f.c, f.ldc, f.r = bufs["c"][i].data_ptr(), lin.n, lin.r.data_ptr()
+            f.M, f.N, f.K, f.a_kind = m, lin.n, lin.k, nat.IMA_FREIVALDS_A_FP8
+            f.mismatch_rows = bufs["mismatch"].data_ptr()
+        return quant, gemm, rows
+
+    def forward(self, xs: list[torch.Tensor], bufs: dict, *, check: bool = True, gemm_only: bool = False) -> None:
         """One forward of every linear on activations xs[i] [tokens, K_i] (bf16).
 
         Writes bufs["c"][i] (exact int64 products), bufs["y"][i] (bf16 outputs) and
         accumulates failed Freivalds rows into bufs["mismatch"].  Launches only."""
+        key = tuple(x.data_ptr() for x in xs)
+        if bufs.get("_key") != key:
+            bufs["_desc"] = self._descriptors(xs, bufs)
+            bufs["_key"] = key
+        quant, gemm, rows = bufs["_desc"]
+        n = len(self.linears)
         lib = nat.lib()
-        dev = self.device
-        stream = nat.stream_of(dev)
-        for i, lin in enumerate(self.linears):
-            x = xs[i]
-            m = int(x.shape[0])
-            q, scale, cs = bufs["q"][i], bufs["scale"][i], bufs["code_scale"][i]
-            planes = bufs["planes"][i]
-            nat.check("ima_quantize_per_token", lib.ima_quantize_per_token(
-                x.data_ptr(), nat.dtype_code(x.dtype), m, lin.k, x.stride(0), q.data_ptr(), lin.k,
-                scale.data_ptr(), None, lin.k, cs.data_ptr(), planes.planes.data_ptr(), planes.ld, stream))
-            c, y = bufs["c"][i], bufs["y"][i]
-            nat.check("ima_int_gemm", lib.ima_int_gemm(
-                planes.planes.data_ptr(), planes.ld, lin.w_planes.planes.data_ptr(), lin.w_planes.ld, m, lin.n, lin.k,
-                nat.IMA_SCHEME_KARATSUBA3, c.data_ptr(), lin.n, cs.data_ptr(), lin.w_code_scale.data_ptr(),
-                nat.ptr(lin.bias), y.data_ptr(), nat.IMA_DTYPE_BF16, lin.n, stream))
-            if check:
-                nat.check("ima_freivalds_fp8", lib.ima_freivalds_fp8(
-                    q.data_ptr(), lin.k, lin.w_fp8.data_ptr(), lin.k, c.data_ptr(), lin.n, lin.r.data_ptr(), m, lin.n,
-                    lin.k, bufs["ws"][i].data_ptr(), bufs["mismatch"].data_ptr(), stream))
+        stream = nat.stream_of(self.device)
+        if not gemm_only:
+            nat.check("ima_quantize_grouped", lib.ima_quantize_grouped(ctypes.byref(quant), n, stream))
+        nat.check("ima_int_gemm_grouped",
+                  lib.ima_int_gemm_grouped(ctypes.byref(gemm), n, nat.IMA_SCHEME_KARATSUBA3, stream))
+        if check and not gemm_only:
+            nat.check("ima_freivalds_rows_grouped", lib.ima_freivalds_rows_grouped(ctypes.byref(rows), n, stream))
 
-    @staticmethod
-    def kernels_per_linear(check: bool = True) -> int:
-        return 4 if check else 2   # quantise, GEMM (+ Freivalds: B r pass, row pass)
+    def launches_per_forward(self, check: bool = True) -> int:
+        gemm = -(-len(self.linears) // self.GEMM_BATCH)
+        return 1 + gemm + (1 if check else 0)
 
 
 class HawkeyeStack:
@@ -136,6 +166,3 @@ class HawkeyeStack:
     @staticmethod
     def kernels_per_linear() -> int:
         return 3
-
-
-__all__ = ["CodebookStack", "HawkeyeStack", "PreparedLinear", "hawkeye_replay", "int_gemm"]

@@ -339,3 +339,74 @@ def test_student_model_end_to_end(cuda_device, monkeypatch, kernel):
         ref = oracle.hawkeye(xq, xs, w0, ws0).to(torch.bfloat16)
         ref = (ref + b0.to(torch.bfloat16)).to(x.dtype)
     assert torch.equal(h.cpu().view(torch.int16), ref.view(torch.int16))
+
+
+# ---------------------------------------------------------------------------
+# grouped launches (many linears per launch) and the prepared pipeline
+# ---------------------------------------------------------------------------
+def test_grouped_pipeline_matches_oracle_and_flags_corruption(cuda_device):
+    from int_model_approximation_b200.pipeline import CodebookStack
+
+    shapes = [(40, 96), (300, 128), (17, 4864), (896, 896), (64, 200)]
+    tokens = 150
+    weights, xs = [], []
+    for i, (n, k) in enumerate(shapes):
+        w, ws = synthetic.normal_fp8_weights(n, k, seed=200 + i)
+        bias = (torch.randn(n, generator=torch.Generator().manual_seed(i)) * 0.1).to(torch.bfloat16)
+        weights.append((w.to(cuda_device), ws.to(cuda_device), bias.to(cuda_device)))
+        xs.append(synthetic.student_t_activations(tokens, k, seed=300 + i).to(cuda_device))
+    stack = CodebookStack(weights)
+    bufs = stack.allocate(tokens)
+    stack.forward(xs, bufs)
+    torch.cuda.synchronize()
+    assert int(bufs["mismatch"].item()) == 0
+    for i, (w, ws, bias) in enumerate(weights):
+        c_ref, _y, out_ref = oracle.codebook_linear(xs[i].cpu(), w.cpu(), ws.cpu(), bias.cpu())
+        assert torch.equal(bufs["c"][i].cpu(), c_ref), f"linear {i}"
+        assert torch.equal(bufs["y"][i].cpu().view(torch.int16), out_ref.view(torch.int16)), f"linear {i}"
+    # corrupt one entry in two products: exactly two rows must be flagged
+    bufs["mismatch"].zero_()
+    bufs["c"][1][7, 3] += 1
+    bufs["c"][3][149, 895] -= 5
+    lib = nat.lib()
+    _q, _g, rows = bufs["_desc"]
+    import ctypes
+    nat.check("rows", lib.ima_freivalds_rows_grouped(ctypes.byref(rows), len(shapes), nat.stream_of(cuda_device)))
+    torch.cuda.synchronize()
+    expected = int(stack.linears[1].r[3].item() != 0) + int(stack.linears[3].r[895].item() != 0)
+    assert int(bufs["mismatch"].item()) == expected == 2
+    _assert_status_clean(cuda_device)
+
+
+def test_grouped_gemm_many_problems_fp32_outputs(cuda_device):
+    """More problems than one launch holds (40), fp32 and bf16 outputs, ragged N."""
+    import ctypes
+
+    probs, refs, keep = [], [], []
+    for i in range(45):
+        m, n, k = 1 + (i * 37) % 200, 8 + (i * 53) % 300, 16 + (i * 29) % 700
+        x = synthetic.student_t_activations(m, k, seed=i)
+        w, ws = synthetic.normal_fp8_weights(n, k, seed=1000 + i)
+        _q, xs, _cb, cs, a = codebook.per_token_fp8(x.to(cuda_device), codebook=True, planes=True)
+        b, _ = codebook.codebook_planes_from_fp8(w.to(cuda_device))
+        wsc = (ws.reshape(-1) / 512.0).to(cuda_device)
+        y_dtype = torch.float32 if i % 2 else torch.bfloat16
+        c = torch.empty((m, n), dtype=torch.int64, device=cuda_device)
+        y = torch.empty((m, n), dtype=y_dtype, device=cuda_device)
+        g = nat.GemmProblem()
+        g.a_planes, g.lda, g.b_planes, g.ldb = a.planes.data_ptr(), a.ld, b.planes.data_ptr(), b.ld
+        g.M, g.N, g.K, g.c, g.ldc = m, n, k, c.data_ptr(), n
+        g.x_scale, g.w_scale, g.bias = cs.reshape(-1).data_ptr(), wsc.data_ptr(), None
+        g.y, g.y_dtype, g.ldy = y.data_ptr(), nat.dtype_code(y_dtype), n
+        probs.append(g)
+        keep += [a, b, c, y, cs, wsc]
+        refs.append((x, w, ws, c, y))
+    arr = (nat.GemmProblem * len(probs))(*probs)
+    nat.check("grouped", nat.lib().ima_int_gemm_grouped(ctypes.byref(arr), len(probs), nat.IMA_SCHEME_KARATSUBA3,
+                                                       nat.stream_of(cuda_device)))
+    torch.cuda.synchronize()
+    for x, w, ws, c, y in refs:
+        c_ref, y_ref, _ = oracle.codebook_linear(x, w, ws)
+        assert torch.equal(c.cpu(), c_ref)
+        assert torch.equal(y.cpu().to(torch.float32).view(torch.int32), y_ref.to(y.dtype).to(torch.float32).view(torch.int32))
+    _assert_status_clean(cuda_device)

@@ -38,6 +38,16 @@ def test_python_binding_covers_header():
     assert lib.ima_status_string(nat.IMA_ERR_TIMEOUT).decode() == "device wait timed out"
 
 
+def test_descriptor_struct_layouts_match_the_header():
+    sizes = (ctypes.c_int64 * 3)()
+    assert nat.lib().ima_struct_sizes(sizes, 3) == 0
+    assert list(sizes) == [
+        ctypes.sizeof(nat.QuantizeProblem),
+        ctypes.sizeof(nat.GemmProblem),
+        ctypes.sizeof(nat.FreivaldsRowsProblem),
+    ]
+
+
 def test_host_only_queries():
     lib = nat.lib()
     assert lib.ima_scheme_planes(nat.IMA_SCHEME_KARATSUBA3) == 6
