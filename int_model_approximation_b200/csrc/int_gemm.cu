@@ -40,7 +40,7 @@ constexpr int GM_BM = 128;
 constexpr int GM_BK = 128;                 // bytes of K per stage (one 128-byte swizzle row)
 constexpr int GM_THREADS = 192;
 constexpr uint32_t GM_TMEM_COLS = 512;
-constexpr int GM_MAXP = 40;                // problems per launch (kernel-parameter budget)
+constexpr int GM_MAXP = 80;                // problems per launch (kernel-parameter budget)
 constexpr int GM_EPI_WARPS = 4;
 
 template <int SCHEME>
@@ -49,7 +49,7 @@ struct Scheme;
 template <>
 struct Scheme<IMA_SCHEME_KARATSUBA3> {
     static constexpr int BN = 64;
-    static constexpr int STAGES = 7;
+    static constexpr int STAGES = 8;
     static constexpr int NACC = 6;
     static constexpr int PRODUCTS = 6;     // stages per K tile
     static constexpr int CHUNK = 16;       // epilogue columns per tcgen05.ld
@@ -92,8 +92,8 @@ struct GemmSmem {
     static constexpr int CST_BYTES = S::TMA_STORE ? 32 * S::CHUNK * 8 : 0;   // 4 KB
     static constexpr int YST_BYTES = S::TMA_STORE ? 32 * S::CHUNK * 4 : 0;   // room for fp32 y
     static constexpr int CST_OFFSET = TILES_BYTES;
-    static constexpr int YST_OFFSET = CST_OFFSET + GM_EPI_WARPS * 2 * CST_BYTES;
-    static constexpr int SCALE_OFFSET = YST_OFFSET + GM_EPI_WARPS * 2 * YST_BYTES;   // ws, bias: [warp][2][BN]
+    static constexpr int YST_OFFSET = CST_OFFSET + GM_EPI_WARPS * CST_BYTES;
+    static constexpr int SCALE_OFFSET = YST_OFFSET + GM_EPI_WARPS * YST_BYTES;   // ws, bias: [warp][2][BN]
     static constexpr int BAR_OFFSET = SCALE_OFFSET + 2 * GM_EPI_WARPS * 2 * BN * 4;
     static constexpr int TOTAL = BAR_OFFSET + (2 * STAGES + 2) * 8 + 16;
     static constexpr int ALLOC = TOTAL + 1024;        // slack to align the base to 1024 B
@@ -111,7 +111,7 @@ struct GemmProblemDev {
 };
 
 struct __align__(64) GemmBatch {
-    CUtensorMap maps[GM_MAXP][4];   // A planes, B planes, C (int64), Y
+    CUtensorMap maps[GM_MAXP][2];   // A planes, B planes
     GemmProblemDev p[GM_MAXP];
     int32_t tile_start[GM_MAXP + 1];
     int32_t n;
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
         // ---------------- epilogue ----------------
         const int ew = warp - 2;               // epilogue warp index 0..3
         const int q = warp & 3;                // TMEM lane quadrant of this warp
-        uint32_t tphase = 0, chunk_ctr = 0, tile_ctr = 0;
+        uint32_t tphase = 0, tile_ctr = 0;
         for (int64_t t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_ctr) {
             const int pi = find_problem(batch, t);
             const GemmProblemDev& P = batch.p[pi];
@@ -289,12 +289,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                 }
                 if constexpr (S::TMA_STORE) {
                     if (tma) {
-                        const int buf = chunk_ctr & 1;
-                        ++chunk_ctr;
-                        unsigned char* cst = smem + L::CST_OFFSET + (ew * 2 + buf) * L::CST_BYTES;
-                        unsigned char* yst = smem + L::YST_OFFSET + (ew * 2 + buf) * L::YST_BYTES;
-                        if (lane == 0) bulk_wait_group_read1();   // the store that last used this buffer has read it
-                        __syncwarp();
+                        unsigned char* cst = smem + L::CST_OFFSET + ew * L::CST_BYTES;
+                        unsigned char* yst = smem + L::YST_OFFSET + ew * L::YST_BYTES;
+                        __syncwarp();   // the previous chunk's copy-out has finished reading the staging
                         if (P.c) {
                             // row `lane` = 128 bytes = 8 chunks of 16 B, chunk j stored at slot j ^ (lane % 8)
 #pragma unroll
@@ -331,12 +328,56 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                                         make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
                             }
                         }
-                        fence_proxy_async_smem();
                         __syncwarp();
-                        if (lane == 0) {
-                            if (P.c) tma_store_2d(&batch.maps[pi][2], cst, n0 + c0, m0 + q * 32);
-                            if (P.y) tma_store_2d(&batch.maps[pi][3], yst, n0 + c0, m0 + q * 32);
-                            bulk_commit_group();
+                        // copy-out: each instruction writes 4 rows x 128 B of C (lanes 8r..8r+7
+                        // read row r's 16-byte slots back through the swizzle) and 16 or 8 rows of y
+                        const int64_t rbase = (int64_t)m0 + q * 32;
+                        const int64_t cbase = (int64_t)n0 + c0;
+                        if (P.c) {
+#pragma unroll
+                            for (int it = 0; it < 8; ++it) {
+                                const int r = it * 4 + (lane >> 3), j = lane & 7;
+                                const int64_t gm = rbase + r, gn = cbase + 2 * j;
+                                const uint4 v = *reinterpret_cast<const uint4*>(cst + r * 128 + ((j ^ (r & 7)) << 4));
+                                if (gm < P.M) {
+                                    int64_t* dst = P.c + gm * P.ldc + gn;
+                                    if (gn + 1 < P.N) {
+                                        *reinterpret_cast<uint4*>(dst) = v;
+                                    } else if (gn < P.N) {
+                                        dst[0] = (int64_t)(((uint64_t)v.y << 32) | v.x);
+                                    }
+                                }
+                            }
+                        }
+                        if (P.y) {
+                            const int esize = P.y_dtype == IMA_DTYPE_F32 ? 4 : 2;
+                            const int row_bytes = S::CHUNK * esize;            // 32 or 64
+                            const int lanes_per_row = row_bytes / 16;           // 2 or 4
+                            const int rows_per_it = 32 / lanes_per_row;         // 16 or 8
+                            for (int it = 0; it < 32 / rows_per_it; ++it) {
+                                const int r = it * rows_per_it + lane / lanes_per_row;
+                                const int part = lane % lanes_per_row;
+                                const int64_t gm = rbase + r;
+                                const int64_t gn = cbase + part * (16 / esize);
+                                const uint4 v = *reinterpret_cast<const uint4*>(yst + r * row_bytes + part * 16);
+                                if (gm < P.M && gn < P.N) {
+                                    unsigned char* dst = reinterpret_cast<unsigned char*>(P.y) + (gm * P.ldy + gn) * esize;
+                                    if (gn + 16 / esize <= P.N) {
+                                        *reinterpret_cast<uint4*>(dst) = v;
+                                    } else if (esize == 4) {
+                                        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                                        for (int e = 0; e < 4; ++e)
+                                            if (gn + e < P.N) reinterpret_cast<uint32_t*>(dst)[e] = w4[e];
+                                    } else {
+                                        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                                        for (int e = 0; e < 8; ++e)
+                                            if (gn + e < P.N)
+                                                reinterpret_cast<uint16_t*>(dst)[e] = (uint16_t)(w4[e >> 1] >> (16 * (e & 1)));
+                                    }
+                                }
+                            }
                         }
                         continue;
                     }
@@ -359,7 +400,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                 }
             }
         }
-        if (S::TMA_STORE && lane == 0) bulk_wait_group_all();   // all stores complete before the CTA exits
     }
     __syncthreads();
     if (warp == 1) {
@@ -396,22 +436,6 @@ int make_plane_map(CUtensorMap* map, const int8_t* base, int64_t ld, int64_t row
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? IMA_OK : IMA_ERR_INVALID_ARGUMENT;
-}
-
-// 2-D store map over an output [rows][cols] with a {16 cols, 32 rows} box.
-bool make_store_map(CUtensorMap* map, void* base, CUtensorMapDataType dt, int esize, int64_t rows, int64_t cols,
-                    int64_t ld, bool swizzle128) {
-    auto enc = get_encode_fn();
-    if (!enc || !base) return false;
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * esize) & 15) || cols < 1 || rows < 1) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
-    cuuint32_t box[2] = {16, 32};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
 }
 
 int num_sms() {
@@ -465,11 +489,13 @@ int run_grouped(const ima_gemm_problem* problems, int count, cudaStream_t stream
     std::stable_sort(order.begin(), order.end(),
                      [&](int a, int b) { return problems[a].K > problems[b].K; });
     static thread_local GemmBatch b;   // host staging of the kernel parameters (copied at launch)
-    size_t i = 0;
-    while (i < order.size()) {
+    // deal the K-sorted problems round-robin into as few launches as the parameter budget
+    // allows, so every launch gets a similar mix of expensive and cheap tiles
+    const size_t nb = (order.size() + GM_MAXP - 1) / GM_MAXP;
+    for (size_t batch = 0; batch < nb; ++batch) {
         memset(&b, 0, sizeof(b));
         int32_t tiles = 0;
-        for (; i < order.size() && b.n < GM_MAXP; ++i) {
+        for (size_t i = batch; i < order.size(); i += nb) {
             const ima_gemm_problem& q = problems[order[i]];
             const int k = b.n;
             GemmProblemDev& D = b.p[k];
@@ -482,17 +508,12 @@ int run_grouped(const ima_gemm_problem* problems, int count, cudaStream_t stream
             D.M = (int32_t)q.M; D.N = (int32_t)q.N; D.K = (int32_t)q.K; D.y_dtype = q.y_dtype;
             D.m_tiles = (int32_t)((q.M + GM_BM - 1) / GM_BM);
             D.k_tiles = (int32_t)((q.K + GM_BK - 1) / GM_BK);
-            bool tma = Scheme<SCHEME>::TMA_STORE;
-            if (tma && q.c)
-                tma = make_store_map(&b.maps[k][2], q.c, CU_TENSOR_MAP_DATA_TYPE_INT64, 8, q.M, q.N, q.ldc, true);
-            if (tma && q.y) {
-                CUtensorMapDataType dt = q.y_dtype == IMA_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                         : q.y_dtype == IMA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-                tma = make_store_map(&b.maps[k][3], q.y, dt, q.y_dtype == IMA_DTYPE_F32 ? 4 : 2, q.M, q.N, q.ldy,
-                                     false);
-            }
-            D.tma_store = tma ? 1 : 0;
+            // staged 16-byte copy-out needs 16-byte aligned rows; otherwise element stores
+            const int yes = q.y_dtype == IMA_DTYPE_F32 ? 4 : 2;
+            bool vec = Scheme<SCHEME>::TMA_STORE;
+            if (q.c) vec = vec && !(reinterpret_cast<uintptr_t>(q.c) & 15) && !((q.ldc * 8) & 15);
+            if (q.y) vec = vec && !(reinterpret_cast<uintptr_t>(q.y) & 15) && !((q.ldy * yes) & 15);
+            D.tma_store = vec ? 1 : 0;
             b.tile_start[k] = tiles;
             tiles += D.m_tiles * (int32_t)((q.N + L::BN - 1) / L::BN);
             b.n = k + 1;

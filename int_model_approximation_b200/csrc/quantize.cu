@@ -68,13 +68,43 @@ struct QuantBatch {
 
 namespace {
 
-// One CTA per (problem, row), grid-stride over all rows of the batch.  Pass 1:
-// NaN-propagating amax.  Pass 2: quantise four consecutive columns per thread-iteration
-// so each plane store is one 32-bit word.
+// Eight consecutive elements of a row as fp32 (zeros beyond K); one or two 16-byte
+// loads when the row and the chunk are 16-byte aligned.
+IMA_DEVINL void load8(const void* row, int dtype, int64_t k0, int64_t K, bool vec, float v[8]) {
+    if (vec && k0 + 8 <= K) {
+        if (dtype == IMA_DTYPE_F32) {
+            const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(row) + k0);
+            float4 a = __ldg(p), b = __ldg(p + 1);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+            uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(row) + k0));
+            uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint16_t lo = (uint16_t)(w[j] & 0xFFFFu), hi = (uint16_t)(w[j] >> 16);
+                if (dtype == IMA_DTYPE_BF16) {
+                    v[2 * j] = ima_bf16_to_f32(lo);
+                    v[2 * j + 1] = ima_bf16_to_f32(hi);
+                } else {
+                    v[2 * j] = __half2float(__ushort_as_half(lo));
+                    v[2 * j + 1] = __half2float(__ushort_as_half(hi));
+                }
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (k0 + j < K) ? load_as_f32(row, dtype, k0 + j) : 0.0f;
+}
+
+// One warp per (problem, row), grid-stride over all rows of the batch.  Pass 1:
+// NaN-propagating amax over 8-element chunks.  Pass 2 (the row is re-read from L1/L2):
+// quantise 8 consecutive columns per lane-iteration, so the code store is 8 bytes and
+// each plane store is one 8-byte word.
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constant__ QuantBatch batch) {
-    __shared__ float s_red[32];
-    __shared__ int s_nan[32];
-    for (int64_t g = blockIdx.x; g < batch.total_rows; g += gridDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps_total = (int64_t)gridDim.x * 8;
+    for (int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); g < batch.total_rows; g += warps_total) {
         int lo = 0, hi = batch.n - 1;
         while (lo < hi) {
             int mid = (lo + hi + 1) >> 1;
@@ -82,72 +112,74 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
         }
         const QuantProblem& P = batch.p[lo];
         const int64_t m = g - P.row_start;
-        const void* x = P.x;
         const int dtype = P.dtype;
-        const int64_t M = P.M, K = P.K, ldx = P.ldx, ldq = P.ldq, ldc = P.ldc, ldp = P.ldp;
-        uint8_t* q = P.q;
-        float* scale_out = P.scale;
-        float* code_scale = P.code_scale;
-        int32_t* codebook = P.codebook;
-        int8_t* planes = P.planes;
+        const int64_t M = P.M, K = P.K, ldq = P.ldq, ldc = P.ldc, ldp = P.ldp;
+        const int esize = dtype == IMA_DTYPE_F32 ? 4 : 2;
+        const unsigned char* row = reinterpret_cast<const unsigned char*>(P.x) + m * P.ldx * esize;
+        const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
+        uint8_t* qrow = P.q + m * ldq;
+        const bool qvec = ((reinterpret_cast<uintptr_t>(qrow) & 7) == 0);
         float amax = 0.0f;
         int has_nan = 0;
-        for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-            float v = fabsf(load_as_f32(x, dtype, m * ldx + k));
-            if (v != v) has_nan = 1;
-            else amax = fmaxf(amax, v);
+        for (int64_t k0 = (int64_t)lane * 8; k0 < K; k0 += 256) {
+            float v[8];
+            load8(row, dtype, k0, K, vec, v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float a = fabsf(v[j]);
+                if (a != a) has_nan = 1;
+                else amax = fmaxf(amax, a);
+            }
         }
         for (int o = 16; o > 0; o >>= 1) {
             amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
             has_nan |= __shfl_xor_sync(0xFFFFFFFFu, has_nan, o);
         }
-        int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-        if (lane == 0) { s_red[warp] = amax; s_nan[warp] = has_nan; }
-        __syncthreads();
-        if (warp == 0) {
-            int nw = blockDim.x >> 5;
-            amax = lane < nw ? s_red[lane] : 0.0f;
-            has_nan = lane < nw ? s_nan[lane] : 0;
-            for (int o = 16; o > 0; o >>= 1) {
-                amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-                has_nan |= __shfl_xor_sync(0xFFFFFFFFu, has_nan, o);
-            }
-            if (lane == 0) { s_red[0] = amax; s_nan[0] = has_nan; }
-        }
-        __syncthreads();
-        float s = s_nan[0] ? __int_as_float(0x7FC00000) : s_red[0];
+        float s = has_nan ? __int_as_float(0x7FC00000) : amax;
         s = __fdiv_rn(s, 448.0f);
         s = (s < 1e-12f) ? 1e-12f : s;   // clamp_min keeps NaN
-        if (threadIdx.x == 0) {
-            scale_out[m] = s;
-            if (code_scale) code_scale[m] = __fdiv_rn(s, 512.0f);
+        if (lane == 0) {
+            P.scale[m] = s;
+            if (P.code_scale) P.code_scale[m] = __fdiv_rn(s, 512.0f);
         }
-        int64_t kq = planes ? ldp : K;   // planes are zero-filled up to ldp
-        for (int64_t k0 = (int64_t)threadIdx.x * 4; k0 < kq; k0 += (int64_t)blockDim.x * 4) {
-            uint32_t word[6] = {0, 0, 0, 0, 0, 0};
+        const int64_t kq = P.planes ? ldp : K;   // planes are zero-filled up to ldp
+        for (int64_t k0 = (int64_t)lane * 8; k0 < kq; k0 += 256) {
+            float v[8];
+            load8(row, dtype, k0, K, vec, v);
+            uint32_t qw[2] = {0, 0};
+            uint32_t pw[6][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}, {0, 0}, {0, 0}};
+            int32_t cv[8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                int64_t k = k0 + j;
-                if (k >= K) break;
-                float f = __fdiv_rn(load_as_f32(x, dtype, m * ldx + k), s);
-                uint8_t b = ima_f32_to_e4m3(f);
-                q[m * ldq + k] = b;
-                int32_t v = ima_e4m3_codebook(b);
-                if (codebook) codebook[m * ldc + k] = v;
-                if (planes) {
-                    int32_t p[6];
-                    karatsuba_planes(v, p);
+            for (int j = 0; j < 8; ++j) {
+                uint32_t b = (k0 + j < K) ? ima_f32_to_e4m3(__fdiv_rn(v[j], s)) : 0u;
+                qw[j >> 2] |= b << (8 * (j & 3));
+                int32_t c = ima_e4m3_codebook(b);
+                cv[j] = c;
+                int32_t p[6];
+                karatsuba_planes(c, p);
 #pragma unroll
-                    for (int i = 0; i < 6; ++i) word[i] |= ((uint32_t)p[i] & 0xFFu) << (8 * j);
+                for (int i = 0; i < 6; ++i) pw[i][j >> 2] |= ((uint32_t)p[i] & 0xFFu) << (8 * (j & 3));
+            }
+            if (k0 < K) {
+                if (qvec && k0 + 8 <= K) {
+                    *reinterpret_cast<uint2*>(qrow + k0) = make_uint2(qw[0], qw[1]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (k0 + j < K) qrow[k0 + j] = (uint8_t)(qw[j >> 2] >> (8 * (j & 3)));
+                }
+                if (P.codebook) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (k0 + j < K) P.codebook[m * ldc + k0 + j] = cv[j];
                 }
             }
-            if (planes) {
+            if (P.planes) {
 #pragma unroll
                 for (int i = 0; i < 6; ++i)
-                    *reinterpret_cast<uint32_t*>(planes + ((int64_t)i * M + m) * ldp + k0) = word[i];
+                    *reinterpret_cast<uint2*>(P.planes + ((int64_t)i * M + m) * ldp + k0) = make_uint2(pw[i][0], pw[i][1]);
             }
         }
-        __syncthreads();
     }
 }
 
@@ -249,7 +281,8 @@ static int check_quant_problem(const ima_quantize_problem& q) {
 
 static int launch_quant(const QuantBatch& b, cudaStream_t s) {
     if (b.total_rows == 0) return IMA_OK;
-    int64_t grid = b.total_rows < 148 * 64 ? b.total_rows : 148 * 64;
+    int64_t grid = (b.total_rows + 7) / 8;   // one warp per row, 8 warps per block
+    if (grid > 148 * 32) grid = 148 * 32;
     quantize_rows_kernel<<<(unsigned)grid, 256, 0, s>>>(b);
     return IMA_LAUNCH_STATUS();
 }

@@ -5,8 +5,8 @@
 weight half of the check t = codebook(W)^T r, both fixed) and runs one forward of all
 of them -- per-token quantisation, the exact int64 GEMM with the fused
 rescale/bias/bf16 epilogue, and the Freivalds row check of every int64 product -- as
-three grouped launches kinds (one quantiser launch, one GEMM launch per 40 linears, one
-Freivalds launch), entirely on the device and without host synchronisation.  The
+grouped launches (one quantiser launch, one GEMM launch per 80 linears, one Freivalds
+launch), entirely on the device and without host synchronisation.  The
 launch sequence can be captured once into a CUDA graph and replayed.
 
 `HawkeyeStack` does the same for the direct Hawkeye replay student.
@@ -38,7 +38,7 @@ class PreparedLinear:
 
 
 class CodebookStack:
-    GEMM_BATCH = 40   # problems per GEMM launch (kernel-parameter budget of the C side)
+    GEMM_BATCH = 80   # problems per GEMM launch (kernel-parameter budget of the C side)
 
     def __init__(self, weights: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]], *, seed: int = 0):
         self.linears: list[PreparedLinear] = []
