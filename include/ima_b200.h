@@ -58,9 +58,9 @@ int ima_device_status(int device, int* code, int* where, int* detail, int clear)
  *   scale [M] fp32 = max(amax_row|x| / 448, 1e-12),
  *   codebook [M,K] int32 = round(q * 512) (optional, row stride ldc),
  *   code_scale [M] fp32 = scale / 512 (optional),
- *   planes [6][M][ldp] int8: the six Karatsuba digit planes of the codebook
- *   values used by ima_int_gemm (optional; ldp >= K, multiple of 16; columns
- *   K..ldp-1 are written as zero). */
+ *   planes [3][M][ldp] int8: the three balanced base-128 digit planes of the codebook
+ *   values (scheme IMA_SCHEME_DIGITS3) used by ima_int_gemm (optional; ldp >= K,
+ *   multiple of 16; columns K..ldp-1 are written as zero). */
 int ima_quantize_per_token(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, uint8_t* q_fp8,
                            int64_t ldq, float* scale, int32_t* codebook, int64_t ldc, float* code_scale,
                            int8_t* planes, int64_t ldp, void* stream);
@@ -88,7 +88,7 @@ int ima_quantize_grouped(const ima_quantize_problem* problems, int count, void* 
 int ima_codebook_from_fp8(const uint8_t* src, int64_t rows, int64_t K, int64_t ld, int32_t* dst, int64_t ldd,
                           void* stream);
 
-/* Karatsuba digit planes of a matrix of e4m3 bytes ([rows,K], row stride ld), e.g. the
+/* DIGITS3 planes of the codebook values of a matrix of e4m3 bytes ([rows,K], row stride ld), e.g. the
  * weight of a CodebookLinear (ref: __main__.py:429-432, done once per linear).
  * codebook_t [K,rows] int32 (optional) receives the transposed codebook the reference
  * keeps as `weight_t`. */
@@ -97,13 +97,15 @@ int ima_planes_from_fp8(const uint8_t* src, int64_t rows, int64_t K, int64_t ld,
 
 /* Digit planes of an int32 matrix given by element strides (stride_row, stride_k), so that
  * both the activation layout [M,K] and the reference's weight_t layout [K,N] can be
- * expanded.  scheme: IMA_SCHEME_KARATSUBA3 (|v| <= 1064960) or IMA_SCHEME_DIGITS5 (any
- * int32).  Values outside the scheme's range set the device status to IMA_ERR_OVERFLOW. */
-#define IMA_SCHEME_KARATSUBA3 3
+ * expanded.  Digits are balanced base-128 (v = sum_i 2^(7 i) d_i); scheme
+ * IMA_SCHEME_DIGITS3 (3 planes, |v| <= 1064960, every codebook value) or
+ * IMA_SCHEME_DIGITS5 (5 planes, any int32).  Values outside the scheme's range set the
+ * device status to IMA_ERR_OVERFLOW. */
+#define IMA_SCHEME_DIGITS3 3
 #define IMA_SCHEME_DIGITS5 5
 int ima_planes_from_int32(const int32_t* src, int64_t rows, int64_t K, int64_t stride_row, int64_t stride_k,
                           int scheme, int8_t* planes, int64_t ldp, void* stream);
-int ima_scheme_planes(int scheme); /* number of planes a scheme uses (6 or 5) */
+int ima_scheme_planes(int scheme); /* number of planes a scheme uses (3 or 5) */
 
 /* Largest |v| over an int32 matrix (device reduction into *out_maxabs, a device int64
  * the caller zeroes).  Used to choose the digit scheme of _int32_matmul. */
@@ -124,7 +126,7 @@ int ima_int_gemm(const int8_t* a_planes, int64_t lda, const int8_t* b_planes, in
                  int64_t K, int scheme, int64_t* c, int64_t ldc, const float* x_scale, const float* w_scale,
                  const float* bias, void* y, int y_dtype, int64_t ldy, void* stream);
 
-/* Many independent products in as few launches as possible (one per 40 problems): every
+/* Many independent products in as few launches as possible (one per 80 problems): every
  * linear of a model in one call.  Fields mean what the arguments of ima_int_gemm mean;
  * all problems use the same digit scheme. */
 typedef struct ima_gemm_problem {

@@ -28,7 +28,7 @@ IMA_DTYPE_F32 = 0
 IMA_DTYPE_BF16 = 1
 IMA_DTYPE_F16 = 2
 
-IMA_SCHEME_KARATSUBA3 = 3
+IMA_SCHEME_DIGITS3 = 3
 IMA_SCHEME_DIGITS5 = 5
 
 _VP = ctypes.c_void_p

@@ -17,7 +17,7 @@ from . import _native as nat
 
 FP8_E4M3_MAX = 448.0
 FP8_E4M3_CODE_SCALE = 512.0
-KARATSUBA3_MAX_ABS = 1_064_960  # largest |v| the three balanced base-128 digits represent
+DIGITS3_MAX_ABS = 1_064_960  # largest |v| the three balanced base-128 digits represent
 
 
 def _round16(k: int) -> int:
@@ -39,7 +39,7 @@ class DigitPlanes:
 
     @staticmethod
     def empty(rows: int, k: int, scheme: int, device: torch.device) -> "DigitPlanes":
-        count = 6 if scheme == nat.IMA_SCHEME_KARATSUBA3 else 5
+        count = 3 if scheme == nat.IMA_SCHEME_DIGITS3 else 5
         planes = torch.empty((count, rows, _round16(k)), dtype=torch.int8, device=device)
         return DigitPlanes(planes, rows, k, scheme)
 
@@ -66,7 +66,7 @@ def per_token_fp8(x: torch.Tensor, *, codebook: bool = False, planes: bool = Fal
     scale = torch.empty((m, 1), dtype=torch.float32, device=dev)
     cb = torch.empty((m, k), dtype=torch.int32, device=dev) if codebook else None
     cs = torch.empty((m, 1), dtype=torch.float32, device=dev) if codebook else None
-    dp = DigitPlanes.empty(m, k, nat.IMA_SCHEME_KARATSUBA3, dev) if planes else None
+    dp = DigitPlanes.empty(m, k, nat.IMA_SCHEME_DIGITS3, dev) if planes else None
     with torch.cuda.device(dev):
         nat.call(
             "ima_quantize_per_token",
@@ -89,14 +89,14 @@ def per_token_fp8(x: torch.Tensor, *, codebook: bool = False, planes: bool = Fal
 
 
 def codebook_planes_from_fp8(w_fp8: torch.Tensor, *, with_codebook_t: bool = False):
-    """Karatsuba digit planes of an e4m3 matrix [rows, K] (a weight, prepared once).
+    """Digit planes (DIGITS3) of the codebook values of an e4m3 matrix [rows, K] (a weight, prepared once).
 
     Optionally also returns the reference's `weight_t` = int32 codebook transposed [K, rows].
     """
     _require_cuda(w_fp8, "FP8 codebook weight")
     w = w_fp8.contiguous().view(torch.uint8)
     rows, k = w.shape
-    dp = DigitPlanes.empty(rows, k, nat.IMA_SCHEME_KARATSUBA3, w.device)
+    dp = DigitPlanes.empty(rows, k, nat.IMA_SCHEME_DIGITS3, w.device)
     cbt = torch.empty((k, rows), dtype=torch.int32, device=w.device) if with_codebook_t else None
     with torch.cuda.device(w.device):
         nat.call(
@@ -123,7 +123,7 @@ def planes_from_int32(t: torch.Tensor, *, transpose: bool = False, scheme: int |
     rows, k = (t.shape[1], t.shape[0]) if transpose else (t.shape[0], t.shape[1])
     sr, sk = (t.stride(1), t.stride(0)) if transpose else (t.stride(0), t.stride(1))
     if scheme is None:
-        scheme = nat.IMA_SCHEME_KARATSUBA3 if int32_maxabs(t) <= KARATSUBA3_MAX_ABS else nat.IMA_SCHEME_DIGITS5
+        scheme = nat.IMA_SCHEME_DIGITS3 if int32_maxabs(t) <= DIGITS3_MAX_ABS else nat.IMA_SCHEME_DIGITS5
     dp = DigitPlanes.empty(rows, k, scheme, t.device)
     with torch.cuda.device(t.device):
         nat.call(

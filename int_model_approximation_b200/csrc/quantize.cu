@@ -6,12 +6,9 @@
 //   code  = round(q * 512)                       exact integer, |code| <= 229376
 //
 // Digit planes.  The GEMM multiplies int8 operands, so each integer operand value v
-// is written in balanced base-128 digits.  Scheme KARATSUBA3 (|v| <= 1,064,960, which
-// covers every codebook value): v = d0 + 2^7 d1 + 2^14 d2 and the six planes
-//     P0 = d0, P1 = d1, P2 = d2, P3 = d0 + d1, P4 = d1 + d2, P5 = d0 + d2
-// all fit int8 (d0, d1 in [-64, 63]); the GEMM forms the six plane products and
-// recombines them Karatsuba-style.  Scheme DIGITS5 (any int32): five digits
-// v = sum_i 2^(7 i) d_i and the 25 digit products are grouped by shift.
+// is written in balanced base-128 digits v = sum_i 2^(7 i) d_i, one int8 plane per digit.
+// Scheme DIGITS3 (|v| <= 1,064,960, which covers every codebook value): three planes
+// d0, d1 in [-64, 63], d2.  Scheme DIGITS5 (any int32): five planes.
 #include "ima_common.cuh"
 
 namespace {
@@ -22,12 +19,8 @@ IMA_DEVINL float load_as_f32(const void* x, int dtype, int64_t idx) {
     return reinterpret_cast<const float*>(x)[idx];
 }
 
-// Six Karatsuba planes of a codebook value (int8 each, packed little-endian per plane).
-IMA_DEVINL void karatsuba_planes(int32_t v, int32_t p[6]) {
-    int32_t d0, d1, d2;
-    ima_digits3(v, d0, d1, d2);
-    p[0] = d0; p[1] = d1; p[2] = d2; p[3] = d0 + d1; p[4] = d1 + d2; p[5] = d0 + d2;
-}
+// The three digit planes of a codebook value.
+IMA_DEVINL void digits3_planes(int32_t v, int32_t p[3]) { ima_digits3(v, p[0], p[1], p[2]); }
 
 IMA_DEVINL void digits5(int32_t v, int32_t d[5]) {
     int64_t w = v;
@@ -147,7 +140,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
             float v[8];
             load8(row, dtype, k0, K, vec, v);
             uint32_t qw[2] = {0, 0};
-            uint32_t pw[6][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}, {0, 0}, {0, 0}};
+            uint32_t pw[3][2] = {{0, 0}, {0, 0}, {0, 0}};
             int32_t cv[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -155,10 +148,10 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
                 qw[j >> 2] |= b << (8 * (j & 3));
                 int32_t c = ima_e4m3_codebook(b);
                 cv[j] = c;
-                int32_t p[6];
-                karatsuba_planes(c, p);
+                int32_t p[3];
+                digits3_planes(c, p);
 #pragma unroll
-                for (int i = 0; i < 6; ++i) pw[i][j >> 2] |= ((uint32_t)p[i] & 0xFFu) << (8 * (j & 3));
+                for (int i = 0; i < 3; ++i) pw[i][j >> 2] |= ((uint32_t)p[i] & 0xFFu) << (8 * (j & 3));
             }
             if (k0 < K) {
                 if (qvec && k0 + 8 <= K) {
@@ -176,7 +169,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
             }
             if (P.planes) {
 #pragma unroll
-                for (int i = 0; i < 6; ++i)
+                for (int i = 0; i < 3; ++i)
                     *reinterpret_cast<uint2*>(P.planes + ((int64_t)i * M + m) * ldp + k0) = make_uint2(pw[i][0], pw[i][1]);
             }
         }
@@ -190,20 +183,20 @@ __global__ void planes_from_fp8_kernel(const uint8_t* __restrict__ src, int64_t 
     int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * words) return;
     int64_t r = idx / words, k0 = (idx % words) * 4;
-    uint32_t word[6] = {0, 0, 0, 0, 0, 0};
+    uint32_t word[3] = {0, 0, 0};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         int64_t k = k0 + j;
         if (k >= K) break;
         int32_t v = ima_e4m3_codebook(src[r * ld + k]);
         if (codebook_t) codebook_t[k * rows + r] = v;
-        int32_t p[6];
-        karatsuba_planes(v, p);
+        int32_t p[3];
+        digits3_planes(v, p);
 #pragma unroll
-        for (int i = 0; i < 6; ++i) word[i] |= ((uint32_t)p[i] & 0xFFu) << (8 * j);
+        for (int i = 0; i < 3; ++i) word[i] |= ((uint32_t)p[i] & 0xFFu) << (8 * j);
     }
 #pragma unroll
-    for (int i = 0; i < 6; ++i) *reinterpret_cast<uint32_t*>(planes + ((int64_t)i * rows + r) * ldp + k0) = word[i];
+    for (int i = 0; i < 3; ++i) *reinterpret_cast<uint32_t*>(planes + ((int64_t)i * rows + r) * ldp + k0) = word[i];
 }
 
 // Planes of a strided int32 matrix.
@@ -214,22 +207,22 @@ __global__ void planes_from_int32_kernel(const int32_t* __restrict__ src, int64_
     int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * words) return;
     int64_t r = idx / words, k0 = (idx % words) * 4;
-    uint32_t word[6] = {0, 0, 0, 0, 0, 0};
-    int np = scheme == IMA_SCHEME_KARATSUBA3 ? 6 : 5;
+    uint32_t word[5] = {0, 0, 0, 0, 0};
+    int np = scheme == IMA_SCHEME_DIGITS3 ? 3 : 5;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         int64_t k = k0 + j;
         if (k >= K) break;
         int32_t v = src[r * stride_row + k * stride_k];
-        int32_t p[6] = {0, 0, 0, 0, 0, 0};
-        if (scheme == IMA_SCHEME_KARATSUBA3) {
+        int32_t p[5] = {0, 0, 0, 0, 0};
+        if (scheme == IMA_SCHEME_DIGITS3) {
             if (v > 1064960 || v < -1064960) ima_record_error(IMA_ERR_OVERFLOW, IMA_WHERE_PLANES, 0);
-            karatsuba_planes(v, p);
+            digits3_planes(v, p);
         } else {
             digits5(v, p);
         }
 #pragma unroll
-        for (int i = 0; i < 6; ++i) word[i] |= ((uint32_t)p[i] & 0xFFu) << (8 * j);
+        for (int i = 0; i < 5; ++i) word[i] |= ((uint32_t)p[i] & 0xFFu) << (8 * j);
     }
     for (int i = 0; i < np; ++i) *reinterpret_cast<uint32_t*>(planes + ((int64_t)i * rows + r) * ldp + k0) = word[i];
 }
@@ -266,7 +259,7 @@ inline unsigned grid_for(int64_t n, int threads) { return (unsigned)((n + thread
 extern "C" {
 
 int ima_scheme_planes(int scheme) {
-    return scheme == IMA_SCHEME_KARATSUBA3 ? 6 : (scheme == IMA_SCHEME_DIGITS5 ? 5 : 0);
+    return scheme == IMA_SCHEME_DIGITS3 ? 3 : (scheme == IMA_SCHEME_DIGITS5 ? 5 : 0);
 }
 
 static int check_quant_problem(const ima_quantize_problem& q) {
@@ -341,7 +334,7 @@ int ima_planes_from_fp8(const uint8_t* src, int64_t rows, int64_t K, int64_t ld,
 int ima_planes_from_int32(const int32_t* src, int64_t rows, int64_t K, int64_t stride_row, int64_t stride_k,
                           int scheme, int8_t* planes, int64_t ldp, void* stream) {
     if (!src || !planes || rows < 0 || K < 0 || ldp < K || ldp % 16 != 0) return IMA_ERR_INVALID_ARGUMENT;
-    if (scheme != IMA_SCHEME_KARATSUBA3 && scheme != IMA_SCHEME_DIGITS5) return IMA_ERR_UNSUPPORTED;
+    if (scheme != IMA_SCHEME_DIGITS3 && scheme != IMA_SCHEME_DIGITS5) return IMA_ERR_UNSUPPORTED;
     if ((reinterpret_cast<uintptr_t>(planes) & 15)) return IMA_ERR_INVALID_ARGUMENT;
     int64_t n = rows * (ldp / 4);
     if (n == 0) return IMA_OK;

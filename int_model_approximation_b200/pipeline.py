@@ -30,7 +30,7 @@ class PreparedLinear:
     n: int
     k: int
     w_fp8: torch.Tensor          # [N, K] e4m3
-    w_planes: DigitPlanes        # Karatsuba planes of codebook(w)
+    w_planes: DigitPlanes        # digit planes of codebook(w)
     w_code_scale: torch.Tensor   # [N] fp32 = weight_scale / 512
     bias: torch.Tensor | None    # [N] fp32
     r: torch.Tensor              # [N] int64 Freivalds vector
@@ -67,7 +67,7 @@ class CodebookStack:
             bufs["q"].append(torch.empty((tokens, lin.k), dtype=torch.uint8, device=dev))
             bufs["scale"].append(torch.empty((tokens,), dtype=torch.float32, device=dev))
             bufs["code_scale"].append(torch.empty((tokens,), dtype=torch.float32, device=dev))
-            bufs["planes"].append(DigitPlanes.empty(tokens, lin.k, nat.IMA_SCHEME_KARATSUBA3, dev))
+            bufs["planes"].append(DigitPlanes.empty(tokens, lin.k, nat.IMA_SCHEME_DIGITS3, dev))
             bufs["c"].append(torch.empty((tokens, lin.n), dtype=torch.int64, device=dev))
             bufs["y"].append(torch.empty((tokens, lin.n), dtype=torch.bfloat16, device=dev))
         bufs["mismatch"] = torch.zeros((1,), dtype=torch.int32, device=dev)
@@ -119,7 +119,7 @@ class CodebookStack:
         if not gemm_only:
             nat.check("ima_quantize_grouped", lib.ima_quantize_grouped(ctypes.byref(quant), n, stream))
         nat.check("ima_int_gemm_grouped",
-                  lib.ima_int_gemm_grouped(ctypes.byref(gemm), n, nat.IMA_SCHEME_KARATSUBA3, stream))
+                  lib.ima_int_gemm_grouped(ctypes.byref(gemm), n, nat.IMA_SCHEME_DIGITS3, stream))
         if check and not gemm_only:
             nat.check("ima_freivalds_rows_grouped", lib.ima_freivalds_rows_grouped(ctypes.byref(rows), n, stream))
 

@@ -307,7 +307,7 @@ def test_inference_mode_keeps_the_codebook_scheme(cuda_device):
     with torch.inference_mode():
         x_i32, _ = students._per_token_fp8_int32(x)
         a, b = students._operand_planes(x_i32, layer.weight_t)
-    assert a.scheme == b.scheme == nat.IMA_SCHEME_KARATSUBA3
+    assert a.scheme == b.scheme == nat.IMA_SCHEME_DIGITS3
 
 
 @pytest.mark.parametrize("kernel", ["codebook", "hawkeye", "hawkeye-class-counts"])
@@ -402,7 +402,7 @@ def test_grouped_gemm_many_problems_fp32_outputs(cuda_device):
         keep += [a, b, c, y, cs, wsc]
         refs.append((x, w, ws, c, y))
     arr = (nat.GemmProblem * len(probs))(*probs)
-    nat.check("grouped", nat.lib().ima_int_gemm_grouped(ctypes.byref(arr), len(probs), nat.IMA_SCHEME_KARATSUBA3,
+    nat.check("grouped", nat.lib().ima_int_gemm_grouped(ctypes.byref(arr), len(probs), nat.IMA_SCHEME_DIGITS3,
                                                        nat.stream_of(cuda_device)))
     torch.cuda.synchronize()
     for x, w, ws, c, y in refs:

@@ -50,7 +50,7 @@ def test_descriptor_struct_layouts_match_the_header():
 
 def test_host_only_queries():
     lib = nat.lib()
-    assert lib.ima_scheme_planes(nat.IMA_SCHEME_KARATSUBA3) == 6
+    assert lib.ima_scheme_planes(nat.IMA_SCHEME_DIGITS3) == 3
     assert lib.ima_scheme_planes(nat.IMA_SCHEME_DIGITS5) == 5
     assert lib.ima_hawkeye_operand_pitch(1) == 128
     assert lib.ima_hawkeye_operand_bytes(100, 33) == 128 * 2 * (32 * 8 + 16 * 4 + 4)

@@ -147,23 +147,30 @@ def test_freivalds_oracle_on_reference_test_matrices():
     assert oracle.freivalds_mismatch_rows(a2, b2, bad, r) == (1 if int(r[5]) != 0 else 0)
 
 
-def test_karatsuba_recombination_is_exact():
-    """The six-plane recombination the GEMM epilogue uses, checked in exact integers."""
-    rng = np.random.default_rng(0)
-    a = rng.integers(-229376, 229377, size=(7, 50), dtype=np.int64)
-    b = rng.integers(-229376, 229377, size=(9, 50), dtype=np.int64)
+def _balanced_digits(v: np.ndarray, count: int) -> list[np.ndarray]:
+    """Balanced base-128 digits as the plane kernels write them (csrc/quantize.cu)."""
+    out = []
+    w = v.astype(np.int64)
+    for _ in range(count - 1):
+        d = ((w + 64) & 127) - 64
+        out.append(d)
+        w = (w - d) >> 7
+    out.append(w)
+    return out
 
-    def planes(v):
-        d0 = ((v + 64) & 127) - 64
-        v1 = (v - d0) >> 7
-        d1 = ((v1 + 64) & 127) - 64
-        d2 = (v1 - d1) >> 7
-        assert np.all(np.abs(d2) <= 63)
-        p = [d0, d1, d2, d0 + d1, d1 + d2, d0 + d2]
-        assert all(np.all((x >= -128) & (x <= 127)) for x in p)
-        return p
 
-    pa, pb = planes(a), planes(b)
-    weights = [1 - 2**7 - 2**14, 2**14 - 2**7 - 2**21, 2**28 - 2**21 - 2**14, 2**7, 2**21, 2**14]
-    c = sum(w * (x @ y.T) for w, x, y in zip(weights, pa, pb))
-    assert np.array_equal(c, a @ b.T)
+@pytest.mark.parametrize("count,lo,hi", [(3, -1_064_960, 1_064_961), (5, -(2**31), 2**31)])
+def test_digit_shift_recombination_is_exact(count, lo, hi):
+    """C = sum_s 2^(7 s) sum_{i+j=s} A_i B_j^T, the GEMM epilogue's recombination,
+    checked in exact integers; every digit fits int8."""
+    rng = np.random.default_rng(count)
+    a = rng.integers(lo, hi, size=(7, 50), dtype=np.int64)
+    b = rng.integers(lo, hi, size=(9, 50), dtype=np.int64)
+    a[0, :3] = [lo, hi - 1, 0]
+    da, db = _balanced_digits(a, count), _balanced_digits(b, count)
+    assert all(np.all((d >= -128) & (d <= 127)) for d in da + db)
+    c = np.zeros((7, 9), dtype=object)
+    for i in range(count):
+        for j in range(count):
+            c = c + (da[i].astype(object) @ db[j].T.astype(object)) * (2 ** (7 * (i + j)))
+    assert np.array_equal(c, a.astype(object) @ b.T.astype(object))
