@@ -196,6 +196,19 @@ int ima_freivalds_rows_grouped(const ima_freivalds_rows_problem* problems, int c
 int ima_freivalds_fp8(const uint8_t* x_fp8, int64_t ldx, const uint8_t* w_fp8, int64_t ldw, const int64_t* c,
                       int64_t ldc, const int64_t* r, int64_t M, int64_t N, int64_t K, void* workspace,
                       int32_t* mismatch_rows, void* stream);
+/* Same check as ima_freivalds_fp8 for callers that cannot allocate device memory (a
+ * verifier inside a process whose device memory is reserved by another allocator, or a
+ * latency-sensitive path that must not pay for cudaMalloc/cudaFree): no workspace
+ * argument, no allocation.  No counterpart in the reference.  The scratch vector lives in
+ * a fixed device array of IMA_FREIVALDS_NOALLOC_MAX_K int64 (512 KiB) that every GPU
+ * loading the library holds until exit; K above that maximum returns IMA_ERR_UNSUPPORTED.
+ * The first call on a device looks the array's address up with that device current.  All
+ * calls on a device share the array (each call clears it first), so calls whose work
+ * overlaps on the GPU race; the caller still zeroes *mismatch_rows. */
+#define IMA_FREIVALDS_NOALLOC_MAX_K 65536
+int ima_freivalds_fp8_noalloc(const uint8_t* x_fp8, int64_t ldx, const uint8_t* w_fp8, int64_t ldw,
+                              const int64_t* c, int64_t ldc, const int64_t* r, int64_t M, int64_t N, int64_t K,
+                              int32_t* mismatch_rows, void* stream);
 /* A int32 [M,K] (row stride lda), B int32 [K,N] (row stride ldb; the reference's weight_t) */
 int ima_freivalds_i32(const int32_t* a, int64_t lda, const int32_t* b, int64_t ldb, const int64_t* c, int64_t ldc,
                       const int64_t* r, int64_t M, int64_t N, int64_t K, void* workspace, int32_t* mismatch_rows,

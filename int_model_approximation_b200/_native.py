@@ -105,6 +105,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _I32,
         [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP],
     ),
+    "ima_freivalds_fp8_noalloc": (
+        _I32,
+        [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP],
+    ),
     "ima_freivalds_i32": (
         _I32,
         [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP],

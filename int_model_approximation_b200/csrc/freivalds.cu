@@ -240,3 +240,60 @@ int ima_freivalds_i32(const int32_t* a, int64_t lda, const int32_t* b, int64_t l
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the codebook Freivalds check.
+//
+// Some callers cannot allocate device memory for the check's scratch vector: a verifier
+// embedded in a process whose device memory is already reserved by another allocator
+// (a framework's caching allocator can hold nearly all of it, so a cudaMalloc from here
+// could fail or fragment that pool), or a latency-sensitive verification path that must
+// not pay for cudaMalloc/cudaFree, which can synchronise the device.  For them the scratch
+// t = codebook(W)^T r lives in a fixed array in this library's device image instead.
+//
+// The array is a host-side stand-in in host code, so its device address is looked up once
+// per device with that device current (cudaGetSymbolAddress) and passed to the kernels.
+// Every GPU that loads the library holds the array (IMA_FREIVALDS_NOALLOC_MAX_K * 8 bytes)
+// until the process exits.  All calls on a device share it and it keeps the last call's
+// contents; the weight pass clears it at the start of each call.  Calls whose work
+// overlaps on the GPU (different streams, or several host threads) race on the array.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned long long g_fv_noalloc_scratch[IMA_FREIVALDS_NOALLOC_MAX_K];
+
+namespace {
+
+constexpr int FV_NOALLOC_MAX_DEVICES = 64;
+std::mutex g_fv_noalloc_mutex;
+unsigned long long* g_fv_noalloc_ptr[FV_NOALLOC_MAX_DEVICES] = {};
+
+// Device address of the scratch array on the current device (looked up on first use).
+int fv_noalloc_scratch(unsigned long long** out) {
+    int dev = -1;
+    int rc = ima_note_cuda(cudaGetDevice(&dev));
+    if (rc != IMA_OK) return rc;
+    if (dev < 0 || dev >= FV_NOALLOC_MAX_DEVICES) return IMA_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_fv_noalloc_mutex);
+    if (!g_fv_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        rc = ima_note_cuda(cudaGetSymbolAddress(&p, g_fv_noalloc_scratch));
+        if (rc != IMA_OK) return rc;
+        if (!p) return IMA_ERR_CUDA;
+        g_fv_noalloc_ptr[dev] = reinterpret_cast<unsigned long long*>(p);
+    }
+    *out = g_fv_noalloc_ptr[dev];
+    return IMA_OK;
+}
+
+}  // namespace
+
+extern "C" int ima_freivalds_fp8_noalloc(const uint8_t* x_fp8, int64_t ldx, const uint8_t* w_fp8, int64_t ldw,
+                                         const int64_t* c, int64_t ldc, const int64_t* r, int64_t M, int64_t N,
+                                         int64_t K, int32_t* mismatch_rows, void* stream) {
+    if (!x_fp8 || !w_fp8 || !c || !r || !mismatch_rows) return IMA_ERR_INVALID_ARGUMENT;
+    if (M < 0 || N < 0 || K < 0 || ldx < K || ldw < K || ldc < N) return IMA_ERR_INVALID_ARGUMENT;
+    if (K > IMA_FREIVALDS_NOALLOC_MAX_K) return IMA_ERR_UNSUPPORTED;   // the fixed scratch holds K <= max
+    unsigned long long* scratch = nullptr;
+    int rc = fv_noalloc_scratch(&scratch);
+    if (rc != IMA_OK) return rc;
+    return ima_freivalds_fp8(x_fp8, ldx, w_fp8, ldw, c, ldc, r, M, N, K, scratch, mismatch_rows, stream);
+}

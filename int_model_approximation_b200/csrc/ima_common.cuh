@@ -9,6 +9,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <string.h>
+#include <mutex>
 
 #include "../../include/ima_b200.h"
 
