@@ -153,6 +153,113 @@ def build_workload(config: int, tokens: int, device, rank: int):
     return shapes, weights, xs
 
 
+def measured_int32_issue_rate(device) -> float:
+    """Integer-ALU instruction throughput of the device (G ops/s) from ima_int32_issue_probe."""
+    from int_model_approximation_b200 import _native as nat
+
+    sink = torch.zeros((256,), dtype=torch.int32, device=device)
+    blocks = 148 * 8
+    iters = 1 << 14
+    stream = torch.cuda.current_stream(device)
+    for _ in range(2):
+        nat.call("ima_int32_issue_probe", iters, blocks, sink.data_ptr(), stream.cuda_stream)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        nat.call("ima_int32_issue_probe", iters, blocks, sink.data_ptr(), stream.cuda_stream)
+        e.record(stream)
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    return blocks * 256 * iters * 16 / (best * 1e-3) / 1e9
+
+
+def run_hawkeye(args, emit: bool = True) -> dict:
+    """Config 2: direct Hawkeye replay of all 168 linears of the 0.5B shapes at
+    `--hawkeye-tokens` tokens (0.1 % x50 outliers).  One step = quantise, stage and replay
+    every linear (captured once in a CUDA graph).  Metric: Hawkeye outputs per second."""
+    from int_model_approximation_b200 import _native as nat
+    from int_model_approximation_b200.hawkeye import HawkeyeOperand
+
+    world, rank, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    lib = nat.lib()
+    tokens = args.hawkeye_tokens
+    shapes, weights, xs = build_workload(2, tokens, device, rank)
+    w_ops = [HawkeyeOperand(w) for w, _ws, _b in weights]
+    w_scales = [ws.reshape(-1).to(torch.float32).contiguous() for _w, ws, _b in weights]
+    kmax = max(s.k for s in shapes)
+    q = torch.empty((tokens, kmax), dtype=torch.uint8, device=device)
+    scale = torch.empty((tokens,), dtype=torch.float32, device=device)
+    xop = torch.empty((int(lib.ima_hawkeye_operand_bytes(tokens, kmax)),), dtype=torch.uint8, device=device)
+    ys = [torch.empty((tokens, s.n), dtype=torch.bfloat16, device=device) for s in shapes]
+    stream = torch.cuda.Stream(device)
+
+    def forward(replay_only: bool = False):
+        sp = stream.cuda_stream
+        for i, s in enumerate(shapes):
+            if not replay_only:
+                x = xs[i]
+                nat.check("q", lib.ima_quantize_per_token(x.data_ptr(), nat.IMA_DTYPE_BF16, tokens, s.k, s.k,
+                                                          q.data_ptr(), s.k, scale.data_ptr(), None, s.k, None,
+                                                          None, 16, sp))
+                nat.check("p", lib.ima_hawkeye_prepare(q.data_ptr(), tokens, s.k, s.k, xop.data_ptr(), sp))
+            nat.check("r", lib.ima_hawkeye_replay(xop.data_ptr(), w_ops[i].buffer.data_ptr(), scale.data_ptr(),
+                                                  w_scales[i].data_ptr(), tokens, s.n, s.k, 32, 14, -139,
+                                                  ys[i].data_ptr(), s.n, None, s.n, sp))
+
+    with torch.cuda.stream(stream):
+        forward()
+    torch.cuda.synchronize()
+    graphs = {}
+    for name, ro in (("step", False), ("replay", True)):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                forward(replay_only=ro)
+        graphs[name] = g
+    steps = max(2, args.hawkeye_steps)
+    times = {}
+    for name, g in graphs.items():
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                g.replay()
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_ev.record(stream)
+            for _ in range(steps):
+                g.replay()
+            e_ev.record(stream)
+        e_ev.synchronize()
+        times[name] = s_ev.elapsed_time(e_ev) / steps
+    outputs = sum(tokens * s.n for s in shapes)
+    products = sum(tokens * s.n * s.k for s in shapes)
+    int_peak = measured_int32_issue_rate(device)
+    replay_terms = products / (times["replay"] * 1e-3)
+    res = {
+        "workload": f"c2: 168 linears of Qwen2.5-0.5B shape, {tokens} tokens, direct Hawkeye K=32 replay",
+        "outputs_per_s": outputs / (times["step"] * 1e-3),
+        "ms_per_step": times["step"],
+        "replay_ms_per_step": times["replay"],
+        "products_per_s": products / (times["step"] * 1e-3),
+        "roofline": {
+            "kernel": "hawkeye_replay_kernel",
+            "bound": "integer/FMA instruction issue",
+            "achieved": round(10.0 * replay_terms / 1e9, 1),
+            "peak": round(int_peak, 1),
+            "unit": "G int ops/s (10 int ops per product, the reference's per-product op count)",
+            "frac": round(10.0 * replay_terms / 1e9 / int_peak, 4),
+            "peak_source": "ima_int32_issue_probe (XOR+ADD chains, all SMs) measured in this run",
+            "products_per_s_replay_only": replay_terms,
+        },
+        "launches_per_step": 3 * len(shapes),
+    }
+    if emit and rank == 0:
+        print(json.dumps({"hawkeye": res}), flush=True)
+    return res
+
+
 def run_profile_step(args) -> None:
     """Two eager forwards of the c1 workload and nothing else: the command profiled by
     ncu for the per-kernel launch list (the second forward is the one summarised)."""
@@ -452,10 +559,15 @@ def main() -> None:
     ap.add_argument("--reference-rows", type=int, default=64)
     ap.add_argument("--profile-step", action="store_true", help="two eager forwards only (for ncu)")
     ap.add_argument("--profile-tokens", type=int, default=TOKENS)
+    ap.add_argument("--hawkeye-only", action="store_true", help="only the config-2 Hawkeye measurement")
+    ap.add_argument("--hawkeye-tokens", type=int, default=16384)
+    ap.add_argument("--hawkeye-steps", type=int, default=3)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.profile_step:
+    if args.hawkeye_only:
+        run_hawkeye(args)
+    elif args.profile_step:
         run_profile_step(args)
     elif args.impl == "reference":
         run_reference(args)

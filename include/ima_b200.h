@@ -45,6 +45,10 @@ int ima_last_cuda_error(void);             /* cudaError_t of the last failing CU
 /* sizeof of the batch descriptor structs below, in declaration order (quantize, gemm,
  * freivalds rows), so that foreign-language bindings can check their layouts. */
 int ima_struct_sizes(int64_t* out, int n);
+/* Diagnostic for the integer-ALU roofline: `blocks` x 256 threads each run `iters`
+ * iterations of 8 interleaved 2-instruction integer chains (XOR + ADD), i.e.
+ * blocks * 256 * iters * 16 integer instructions; time it with events on `stream`. */
+int ima_int32_issue_probe(int64_t iters, int blocks, uint32_t* sink, void* stream);
 
 /* Reads (synchronously: waits for the device) and optionally clears the device status
  * word of `device`.  code == IMA_OK when no kernel recorded a failure. */

@@ -29,6 +29,34 @@ const char* ima_status_string(int status) {
 
 int ima_last_cuda_error(void) { return g_last_cuda_error; }
 
+}  // extern "C"
+
+// Issue-rate probe for the integer ALU roofline: every thread runs 8 independent
+// LOP3/IADD3 chains, so the kernel is bound by integer instruction issue alone.
+__global__ void __launch_bounds__(256) int32_issue_probe_kernel(int64_t iters, uint32_t seed, uint32_t* sink) {
+    uint32_t a[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = seed + threadIdx.x * 8 + j;
+    for (int64_t i = 0; i < iters; ++i) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            a[j] = (a[j] ^ a[(j + 1) & 7]) + a[(j + 3) & 7];
+        }
+    }
+    uint32_t r = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r ^= a[j];
+    if (r == 0x12345678u) sink[threadIdx.x] = r;   // practically never; keeps the chains alive
+}
+
+extern "C" {
+
+int ima_int32_issue_probe(int64_t iters, int blocks, uint32_t* sink, void* stream) {
+    if (iters <= 0 || blocks <= 0 || !sink) return IMA_ERR_INVALID_ARGUMENT;
+    int32_issue_probe_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(iters, 0x9E3779B9u, sink);
+    return IMA_LAUNCH_STATUS();
+}
+
 int ima_struct_sizes(int64_t* out, int n) {
     if (!out || n < 3) return IMA_ERR_INVALID_ARGUMENT;
     out[0] = (int64_t)sizeof(ima_quantize_problem);
