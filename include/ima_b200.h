@@ -49,6 +49,16 @@ int ima_struct_sizes(int64_t* out, int n);
  * iterations of 8 interleaved 2-instruction integer chains (XOR + ADD), i.e.
  * blocks * 256 * iters * 16 integer instructions; time it with events on `stream`. */
 int ima_int32_issue_probe(int64_t iters, int blocks, uint32_t* sink, void* stream);
+/* Self-test of the quantiser's fast path (no reference counterpart).  Adds to
+ * *mismatches (device memory, zeroed by the caller) the number of disagreements:
+ * kind 0 - the hardware e4m3 cast vs the torch-shaped software cast on every fp32
+ * value with |f| < 464; kind 1 / 2 - for every positive finite bf16 / fp16 amax
+ * (s = max(amax/448, 1e-12)) and every bf16 / fp16 element x with |x| <= amax, the e4m3
+ * code of the corrected-reciprocal quotient vs the code of the IEEE quotient x / s;
+ * kind 3 / 4 - the same pairs, the fp32 quotients themselves wherever x / s is a normal
+ * number and |x| >= 2^-100 (no underflow in the correction step).  A correct build
+ * reports 0 for every kind. */
+int ima_quant_fast_selftest(int kind, unsigned long long* mismatches, void* stream);
 
 /* Reads (synchronously: waits for the device) and optionally clears the device status
  * word of `device`.  code == IMA_OK when no kernel recorded a failure. */

@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ima_abi_version": (_I32, []),
     "ima_struct_sizes": (_I32, [_VP, _I32]),
     "ima_int32_issue_probe": (_I32, [_I64, _I32, _VP, _VP]),
+    "ima_quant_fast_selftest": (_I32, [_I32, _VP, _VP]),
     "ima_quantize_grouped": (_I32, [_VP, _I32, _VP]),
     "ima_int_gemm_grouped": (_I32, [_VP, _I32, _I32, _VP]),
     "ima_freivalds_weight_vector": (_I32, [_VP, _I64, _VP, _I64, _I64, _VP, _VP]),

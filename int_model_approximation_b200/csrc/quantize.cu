@@ -90,10 +90,61 @@ IMA_DEVINL void load8(const void* row, int dtype, int64_t k0, int64_t K, bool ve
     for (int j = 0; j < 8; ++j) v[j] = (k0 + j < K) ? load_as_f32(row, dtype, k0 + j) : 0.0f;
 }
 
+// ---------------------------------------------------------------------------
+// Fast per-element path for rows whose scale s is finite.
+//
+// Division.  Markstein's correction (P. Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990):
+// with y = RN(1/s) and q0 = RN(x y), the residual r = x - s q0 is exact and
+// RN(q0 + r y) is the correctly rounded quotient RN(x / s).  It is used for bf16 and
+// fp16 inputs, whose every (row scale, element) pair ima_quant_fast_selftest checks
+// against IEEE division; fp32 inputs keep __fdiv_rn.
+//
+// e4m3.  The hardware cvt.rn.satfinite.e4m3x2.f32 rounds to nearest even like
+// torch's cast; the two differ only for |f| >= 464 (torch gives NaN, satfinite
+// clamps) and NaN signs.  With a finite scale |x / s| <= 448.00003, and
+// ima_quant_fast_selftest checks the two casts on every fp32 value with |f| < 464.
+// Rows with a NaN or infinite scale take the exact reference-shaped path instead.
+// ---------------------------------------------------------------------------
+// (computed on |x| with x's sign restored, so that -0 / s stays -0)
+IMA_DEVINL float qz_div(float x, float s, float y) {
+    const float ax = fabsf(x);
+    const float q0 = __fmul_rn(ax, y);
+    const float r = __fmaf_rn(-q0, s, ax);
+    const float q = __fmaf_rn(r, y, q0);
+    return __uint_as_float(__float_as_uint(q) | (__float_as_uint(x) & 0x80000000u));
+}
+
+IMA_DEVINL uint32_t qz_cvt_e4m3x2(float lo, float hi) {
+    uint16_t d;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(hi), "f"(lo));
+    return d;   // lo in bits 0..7, hi in bits 8..15
+}
+
+// round(e4m3 * 512) of a non-NaN e4m3 byte
+IMA_DEVINL int32_t qz_codebook(uint32_t b) {
+    const uint32_t e = (b >> 3) & 15u, m = b & 7u;
+    const int32_t v = (int32_t)((e ? (m | 8u) : m) << (e ? e - 1u : 0u));
+    const int32_t sg = -(int32_t)((b >> 7) & 1u);
+    return (v ^ sg) - sg;
+}
+
+// NaN-propagating max of packed |bf16| / |f16| pairs
+IMA_DEVINL uint32_t qz_absmax2(uint32_t acc, uint32_t w, bool bf16) {
+    uint32_t a = w & 0x7FFF7FFFu, d;
+    if (bf16) asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(acc), "r"(a));
+    else asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(d) : "r"(acc), "r"(a));
+    return d;
+}
+
+IMA_DEVINL float qz_half_to_f32(uint32_t h, bool bf16) {
+    return bf16 ? __uint_as_float(h << 16) : __half2float(__ushort_as_half((unsigned short)h));
+}
+
 // One warp per (problem, row), grid-stride over all rows of the batch.  Pass 1:
-// NaN-propagating amax over 8-element chunks.  Pass 2 (the row is re-read from L1/L2):
-// quantise 8 consecutive columns per lane-iteration, so the code store is 8 bytes and
-// each plane store is one 8-byte word.
+// NaN-propagating amax (packed pairs for bf16/fp16).  Pass 2 (the row is re-read
+// from L1/L2): quantise 8 consecutive columns per lane-iteration, so the code store
+// is 8 bytes and each plane store is one 8-byte word.
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constant__ QuantBatch batch) {
     const int lane = threadIdx.x & 31;
     const int64_t warps_total = (int64_t)gridDim.x * 8;
@@ -107,21 +158,42 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
         const int64_t m = g - P.row_start;
         const int dtype = P.dtype;
         const int64_t M = P.M, K = P.K, ldq = P.ldq, ldc = P.ldc, ldp = P.ldp;
-        const int esize = dtype == IMA_DTYPE_F32 ? 4 : 2;
-        const unsigned char* row = reinterpret_cast<const unsigned char*>(P.x) + m * P.ldx * esize;
+        const bool half = dtype != IMA_DTYPE_F32, bf16 = dtype == IMA_DTYPE_BF16;
+        const unsigned char* row = reinterpret_cast<const unsigned char*>(P.x) + m * P.ldx * (half ? 2 : 4);
         const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
         uint8_t* qrow = P.q + m * ldq;
         const bool qvec = ((reinterpret_cast<uintptr_t>(qrow) & 7) == 0);
+
+        // ---- pass 1: amax ----
         float amax = 0.0f;
         int has_nan = 0;
-        for (int64_t k0 = (int64_t)lane * 8; k0 < K; k0 += 256) {
-            float v[8];
-            load8(row, dtype, k0, K, vec, v);
+        if (half) {
+            uint32_t mx2 = 0;
+            const uint16_t* hrow = reinterpret_cast<const uint16_t*>(row);
+            for (int64_t k0 = (int64_t)lane * 8; k0 < K; k0 += 256) {
+                if (vec && k0 + 8 <= K) {
+                    const uint4 u = __ldg(reinterpret_cast<const uint4*>(hrow + k0));
+                    mx2 = qz_absmax2(mx2, u.x, bf16);
+                    mx2 = qz_absmax2(mx2, u.y, bf16);
+                    mx2 = qz_absmax2(mx2, u.z, bf16);
+                    mx2 = qz_absmax2(mx2, u.w, bf16);
+                } else {
+                    for (int j = 0; j < 8 && k0 + j < K; ++j) mx2 = qz_absmax2(mx2, hrow[k0 + j], bf16);
+                }
+            }
+            const float a0 = qz_half_to_f32(mx2 & 0xFFFFu, bf16), a1 = qz_half_to_f32(mx2 >> 16, bf16);
+            has_nan = (a0 != a0) || (a1 != a1);
+            amax = fmaxf(a0, a1);
+        } else {
+            for (int64_t k0 = (int64_t)lane * 8; k0 < K; k0 += 256) {
+                float v[8];
+                load8(row, dtype, k0, K, vec, v);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                float a = fabsf(v[j]);
-                if (a != a) has_nan = 1;
-                else amax = fmaxf(amax, a);
+                for (int j = 0; j < 8; ++j) {
+                    float a = fabsf(v[j]);
+                    if (a != a) has_nan = 1;
+                    else amax = fmaxf(amax, a);
+                }
             }
         }
         for (int o = 16; o > 0; o >>= 1) {
@@ -135,23 +207,49 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
             P.scale[m] = s;
             if (P.code_scale) P.code_scale[m] = __fdiv_rn(s, 512.0f);
         }
+        const bool finite = fabsf(s) <= 3.402823466e38f;   // false for NaN and inf
+        const bool markstein = finite && half;
+        const float y = __frcp_rn(s);
+
+        // ---- pass 2: e4m3 codes, codebook values, digit planes ----
         const int64_t kq = P.planes ? ldp : K;   // planes are zero-filled up to ldp
         for (int64_t k0 = (int64_t)lane * 8; k0 < kq; k0 += 256) {
             float v[8];
             load8(row, dtype, k0, K, vec, v);
-            uint32_t qw[2] = {0, 0};
-            uint32_t pw[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+            uint32_t qw[2];
+            if (finite) {
+                float qv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) qv[j] = markstein ? qz_div(v[j], s, y) : __fdiv_rn(v[j], s);
+                qw[0] = qz_cvt_e4m3x2(qv[0], qv[1]) | (qz_cvt_e4m3x2(qv[2], qv[3]) << 16);
+                qw[1] = qz_cvt_e4m3x2(qv[4], qv[5]) | (qz_cvt_e4m3x2(qv[6], qv[7]) << 16);
+                if (k0 + 8 > K) {   // ragged tail: codes beyond K are zero
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (k0 + j >= K) qw[j >> 2] &= ~(0xFFu << (8 * (j & 3)));
+                }
+            } else {
+                qw[0] = qw[1] = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t b = (k0 + j < K) ? ima_f32_to_e4m3(__fdiv_rn(v[j], s)) : 0u;
+                    qw[j >> 2] |= b << (8 * (j & 3));
+                }
+            }
             int32_t cv[8];
+            uint32_t pw[3][2] = {{0, 0}, {0, 0}, {0, 0}};
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                uint32_t b = (k0 + j < K) ? ima_f32_to_e4m3(__fdiv_rn(v[j], s)) : 0u;
-                qw[j >> 2] |= b << (8 * (j & 3));
-                int32_t c = ima_e4m3_codebook(b);
+                const uint32_t b = (qw[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+                const int32_t c = finite ? qz_codebook(b) : ima_e4m3_codebook(b);
                 cv[j] = c;
-                int32_t p[3];
-                digits3_planes(c, p);
-#pragma unroll
-                for (int i = 0; i < 3; ++i) pw[i][j >> 2] |= ((uint32_t)p[i] & 0xFFu) << (8 * (j & 3));
+                // balanced base-128 digits: u = c + 64 + 64 * 128 has digits (d0+64, d1+64, d2)
+                const int32_t u = c + 8256;
+                const uint32_t d0 = (uint32_t)((u & 127) - 64), d1 = (uint32_t)(((u >> 7) & 127) - 64);
+                const uint32_t d2 = (uint32_t)(u >> 14);
+                pw[0][j >> 2] |= (d0 & 0xFFu) << (8 * (j & 3));
+                pw[1][j >> 2] |= (d1 & 0xFFu) << (8 * (j & 3));
+                pw[2][j >> 2] |= (d2 & 0xFFu) << (8 * (j & 3));
             }
             if (k0 < K) {
                 if (qvec && k0 + 8 <= K) {
@@ -174,6 +272,47 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
             }
         }
     }
+}
+
+// Self-test of the fast path (no reference counterpart; run by the GPU tests).
+//   kind 0: every fp32 value |f| < 464: hardware cvt vs ima_f32_to_e4m3
+//   kind 1 / 2: every positive finite bf16 (1) / fp16 (2) amax and every element x of
+//     that type with |x| <= amax (the pairs a row can hold): the e4m3 code of the fast
+//     quotient vs ima_f32_to_e4m3(__fdiv_rn(x, s)), with the kernel's own scale formula
+//   kind 3 / 4: the same pairs, the fp32 quotient itself vs __fdiv_rn wherever the
+//     theorem's no-underflow condition holds: a normal quotient and |x| >= 2^-100, so
+//     that the residual x - s q0 (about |x| 2^-24) is a normal number.  Below that the
+//     quotients are many binades under the e4m3 range, where kinds 1 / 2 cover them.
+__global__ void quant_fast_selftest_kernel(int kind, unsigned long long* __restrict__ mismatches) {
+    unsigned long long bad = 0;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    if (kind == 0) {
+        for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (1ull << 32); i += stride) {
+            const float f = __uint_as_float((uint32_t)i);
+            if (!(fabsf(f) < 464.0f)) continue;
+            const uint32_t hw = qz_cvt_e4m3x2(f, 0.0f) & 0xFFu;
+            if (hw != ima_f32_to_e4m3(f)) ++bad;
+        }
+    } else {
+        const bool bf16 = kind == 1 || kind == 3, codes = kind <= 2;
+        for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (1ull << 31); i += stride) {
+            const uint32_t ha = (uint32_t)(i >> 16) & 0x7FFFu, hx = (uint32_t)i & 0xFFFFu;
+            const float amax = qz_half_to_f32(ha, bf16), x = qz_half_to_f32(hx, bf16);
+            if (!(amax > 0.0f) || !(amax <= 3.402823466e38f) || !(fabsf(x) <= amax)) continue;
+            float s = __fdiv_rn(amax, 448.0f);
+            s = (s < 1e-12f) ? 1e-12f : s;
+            const float y = __frcp_rn(s);
+            const float fast = qz_div(x, s, y), ieee = __fdiv_rn(x, s);
+            if (codes) {
+                if ((qz_cvt_e4m3x2(fast, 0.0f) & 0xFFu) != ima_f32_to_e4m3(ieee)) ++bad;
+            } else if (fabsf(x) >= 0x1p-100f && fabsf(ieee) >= 1.17549435e-38f &&
+                       __float_as_uint(fast) != __float_as_uint(ieee)) {
+                ++bad;
+            }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) bad += __shfl_xor_sync(0xFFFFFFFFu, bad, o);
+    if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
 // Planes of an e4m3 matrix (weights): one thread per 4 consecutive columns.
@@ -257,6 +396,12 @@ inline unsigned grid_for(int64_t n, int threads) { return (unsigned)((n + thread
 }  // namespace
 
 extern "C" {
+
+int ima_quant_fast_selftest(int kind, unsigned long long* mismatches, void* stream) {
+    if (kind < 0 || kind > 4 || !mismatches) return IMA_ERR_INVALID_ARGUMENT;
+    quant_fast_selftest_kernel<<<148 * 16, 256, 0, (cudaStream_t)stream>>>(kind, mismatches);
+    return IMA_LAUNCH_STATUS();
+}
 
 int ima_scheme_planes(int scheme) {
     return scheme == IMA_SCHEME_DIGITS3 ? 3 : (scheme == IMA_SCHEME_DIGITS5 ? 5 : 0);

@@ -77,6 +77,56 @@ def test_quantiser_random_rows_against_oracle(cuda_device, dtype):
     assert torch.equal(cb.cpu(), oracle.fp8_codebook(q_ref))
 
 
+@pytest.mark.parametrize("kind", [0, 1, 2, 3, 4])
+def test_quantiser_fast_path_selftest(cuda_device, kind):
+    """Exhaustive on-device check of the quantiser's fast path against the torch-shaped
+    software cast and IEEE division: the hardware e4m3 cast on every fp32 value below 464
+    in magnitude (kind 0); the e4m3 codes (kinds 1, 2) and the normal fp32 quotients
+    (kinds 3, 4) of the corrected-reciprocal division on every (amax, element) pair a
+    bf16 / fp16 row can hold."""
+    bad = torch.zeros(1, dtype=torch.int64, device=cuda_device)
+    nat.call("ima_quant_fast_selftest", kind, bad.data_ptr(), nat.stream_of(cuda_device))
+    assert int(bad.item()) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_quantiser_special_rows_and_planes(cuda_device, dtype):
+    """Rows with NaN, +-inf, all zeros, tiny (subnormal) values and a ragged K.  Codes are
+    compared bit for bit with the reference's expression (__main__.py:148-154) evaluated by
+    torch on CUDA, the platform the reference quantises on, and with the CPU oracle up to
+    the sign of NaN codes: an invalid division (inf / inf) yields x86's negative default
+    NaN on the CPU but CUDA's positive canonical NaN on the GPU.  The digit planes rebuild
+    the codebook and are zero beyond K."""
+    m, k = 12, 903
+    x = synthetic.student_t_activations(m, k, seed=9, outlier_fraction=0.02, dtype=torch.float32)
+    x[1, 17] = float("nan")
+    x[2, 5] = float("inf")
+    x[3, 100] = float("-inf")
+    x[4] = 0.0
+    x[5] = x[5] * 1e-38
+    x[6, :3] = torch.tensor([65504.0, -1e-7, 3e-8])
+    x = x.to(dtype)
+    xd = x.to(cuda_device)
+    q, scale, cb, _cs, dp = codebook.per_token_fp8(xd, codebook=True, planes=True)
+    s_cuda = (xd.float().abs().amax(dim=1, keepdim=True) / 448.0).clamp_min(1e-12)
+    q_cuda = (xd.float() / s_cuda).to(torch.float8_e4m3fn)
+    assert torch.equal(q.view(torch.uint8), q_cuda.view(torch.uint8))
+    q_ref, s_ref = oracle.per_token_fp8(x)
+    unsigned_nan = (q.view(torch.uint8).cpu() & 0x7F) == 0x7F
+    assert torch.equal(unsigned_nan, (q_ref.view(torch.uint8) & 0x7F) == 0x7F)
+    same = (q.view(torch.uint8).cpu() == q_ref.view(torch.uint8)) | unsigned_nan
+    assert bool(same.all())
+    nan = torch.isnan(scale.cpu().reshape(-1))
+    assert torch.equal(nan, torch.isnan(s_ref.reshape(-1)))   # NaN payloads are platform-defined
+    assert np.array_equal(_bits(scale.reshape(-1))[~nan.numpy()], _bits(s_ref.reshape(-1))[~nan.numpy()])
+    assert torch.equal(cb.cpu(), oracle.fp8_codebook(q_ref))
+    p = dp.planes.cpu().to(torch.int64)
+    assert p.shape[0] == 3 and p.shape[1] == m and p.shape[2] >= k
+    assert torch.equal(p[0, :, :k] + 128 * p[1, :, :k] + 16384 * p[2, :, :k], cb.cpu().to(torch.int64))
+    assert int(p[:2].min()) >= -64 and int(p[:2].max()) <= 63
+    assert not p[:, :, k:].any()
+
+
 # ---------------------------------------------------------------------------
 # Hawkeye replay
 # ---------------------------------------------------------------------------
