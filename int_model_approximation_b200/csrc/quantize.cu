@@ -141,11 +141,116 @@ IMA_DEVINL float qz_half_to_f32(uint32_t h, bool bf16) {
     return bf16 ? __uint_as_float(h << 16) : __half2float(__ushort_as_half((unsigned short)h));
 }
 
-// One warp per (problem, row), grid-stride over all rows of the batch.  Pass 1:
-// NaN-propagating amax (packed pairs for bf16/fp16).  Pass 2 (the row is re-read
-// from L1/L2): quantise 8 consecutive columns per lane-iteration, so the code store
-// is 8 bytes and each plane store is one 8-byte word.
-__global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constant__ QuantBatch batch) {
+// Eight consecutive 16-bit elements of a row as raw bits (zeros beyond K): one 16-byte
+// load when the row is 16-byte aligned and the chunk is whole.
+IMA_DEVINL uint4 qz_load_half8(const uint16_t* row, int64_t k0, int64_t K, bool vec) {
+    if (vec && k0 + 8 <= K) return __ldg(reinterpret_cast<const uint4*>(row + k0));
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (k0 + j < K) w[j >> 1] |= (uint32_t)__ldg(row + k0 + j) << (16 * (j & 1));
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+IMA_DEVINL void qz_unpack_half8(uint4 u, bool bf16, float v[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (bf16) {
+            v[2 * j] = __uint_as_float(w[j] << 16);
+            v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+        } else {
+            v[2 * j] = __half2float(__ushort_as_half((unsigned short)(w[j] & 0xFFFFu)));
+            v[2 * j + 1] = __half2float(__ushort_as_half((unsigned short)(w[j] >> 16)));
+        }
+    }
+}
+
+// Output pointers of one row, hoisted out of the batch descriptor.
+struct QzRow {
+    uint8_t* q;          // e4m3 codes
+    int32_t* cb;         // codebook values (optional)
+    int8_t* pl;          // plane 0 of the row (optional); plane i at pl + i * pstride
+    int64_t pstride;
+    int64_t K;
+    bool qvec;           // q row 8-byte aligned
+};
+
+// e4m3 codes of eight columns by the fast path (finite scale, half-precision input).
+IMA_DEVINL uint2 qz_codes_fast(const float v[8], float s, float y) {
+    float qv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qv[j] = qz_div(v[j], s, y);
+    return make_uint2(qz_cvt_e4m3x2(qv[0], qv[1]) | (qz_cvt_e4m3x2(qv[2], qv[3]) << 16),
+                      qz_cvt_e4m3x2(qv[4], qv[5]) | (qz_cvt_e4m3x2(qv[6], qv[7]) << 16));
+}
+
+// e4m3 codes of eight columns with IEEE division: fp32 inputs (hardware cast when the
+// scale is finite) and rows with a NaN or infinite scale (torch-shaped software cast).
+// Columns at or beyond `valid` give code 0.
+IMA_DEVINL uint2 qz_codes_ieee(const float v[8], float s, bool finite, int64_t valid) {
+    uint32_t qw[2] = {0, 0};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float q = __fdiv_rn(v[j], s);
+        uint32_t b = finite ? (qz_cvt_e4m3x2(q, 0.0f) & 0xFFu) : ima_f32_to_e4m3(q);
+        if (j >= valid) b = 0;
+        qw[j >> 2] |= b << (8 * (j & 3));
+    }
+    return make_uint2(qw[0], qw[1]);
+}
+
+// Store the codes of columns k0..k0+7, their codebook values and their digit planes.
+// lut[b] packs the three digit bytes of the codebook value of e4m3 byte b; code[b] is
+// that value (NaN codes give 0, as in ima_e4m3_codebook).  Columns >= K hold code 0
+// (digits 0), which the planes carry up to their zero-filled width.
+IMA_DEVINL void qz_emit(const QzRow& R, int64_t k0, uint2 qv, const uint32_t* lut, const int32_t* code) {
+    const uint32_t qw[2] = {qv.x, qv.y};
+    if (k0 < R.K) {
+        if (R.qvec && k0 + 8 <= R.K) {
+            *reinterpret_cast<uint2*>(R.q + k0) = qv;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (k0 + j < R.K) R.q[k0 + j] = (uint8_t)(qw[j >> 2] >> (8 * (j & 3)));
+        }
+        if (R.cb) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (k0 + j < R.K) R.cb[k0 + j] = code[__byte_perm(qw[j >> 2], 0, 0x4440 | (j & 3))];
+        }
+    }
+    if (R.pl) {
+        uint32_t L[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) L[j] = lut[__byte_perm(qw[j >> 2], 0, 0x4440 | (j & 3))];
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const uint32_t sel = (uint32_t)i | ((uint32_t)(4 + i) << 4);   // byte i of x, byte i of y
+            const uint32_t w0 = __byte_perm(__byte_perm(L[0], L[1], sel), __byte_perm(L[2], L[3], sel), 0x5410);
+            const uint32_t w1 = __byte_perm(__byte_perm(L[4], L[5], sel), __byte_perm(L[6], L[7], sel), 0x5410);
+            *reinterpret_cast<uint2*>(R.pl + i * R.pstride + k0) = make_uint2(w0, w1);
+        }
+    }
+}
+
+// One warp per (problem, row), grid-stride over all rows of the batch.  Pass 1: the
+// NaN-propagating amax, with four 16-byte loads in flight per lane (packed pairs for
+// bf16/fp16); a row of at most 1024 half-precision elements stays in registers for
+// pass 2, longer rows are re-read from L2.  Pass 2 quantises eight consecutive columns
+// per lane and chunk, so the code store is 8 bytes and each plane store one 8-byte word.
+__global__ void __launch_bounds__(256, 3) quantize_rows_kernel(const __grid_constant__ QuantBatch batch) {
+    __shared__ uint32_t s_lut[256];
+    __shared__ int32_t s_code[256];
+    {
+        const uint32_t b = threadIdx.x;   // blockDim.x == 256
+        const int32_t c = ima_e4m3_codebook(b);
+        const int32_t u = c + 8256;       // digits of u are (d0 + 64, d1 + 64, d2)
+        s_code[b] = c;
+        s_lut[b] = ((uint32_t)((u & 127) - 64) & 0xFFu) | (((uint32_t)(((u >> 7) & 127) - 64) & 0xFFu) << 8) |
+                   (((uint32_t)(u >> 14) & 0xFFu) << 16);
+    }
+    __syncthreads();
     const int lane = threadIdx.x & 31;
     const int64_t warps_total = (int64_t)gridDim.x * 8;
     for (int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); g < batch.total_rows; g += warps_total) {
@@ -157,28 +262,31 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
         const QuantProblem& P = batch.p[lo];
         const int64_t m = g - P.row_start;
         const int dtype = P.dtype;
-        const int64_t M = P.M, K = P.K, ldq = P.ldq, ldc = P.ldc, ldp = P.ldp;
+        const int64_t K = P.K;
         const bool half = dtype != IMA_DTYPE_F32, bf16 = dtype == IMA_DTYPE_BF16;
         const unsigned char* row = reinterpret_cast<const unsigned char*>(P.x) + m * P.ldx * (half ? 2 : 4);
+        const uint16_t* hrow = reinterpret_cast<const uint16_t*>(row);
         const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
-        uint8_t* qrow = P.q + m * ldq;
-        const bool qvec = ((reinterpret_cast<uintptr_t>(qrow) & 7) == 0);
+        const bool qvec = ((reinterpret_cast<uintptr_t>(P.q + m * P.ldq) & 7) == 0);
+        const bool resident = half && K <= 1024;
 
         // ---- pass 1: amax ----
         float amax = 0.0f;
         int has_nan = 0;
+        uint4 keep[4];
         if (half) {
             uint32_t mx2 = 0;
-            const uint16_t* hrow = reinterpret_cast<const uint16_t*>(row);
-            for (int64_t k0 = (int64_t)lane * 8; k0 < K; k0 += 256) {
-                if (vec && k0 + 8 <= K) {
-                    const uint4 u = __ldg(reinterpret_cast<const uint4*>(hrow + k0));
-                    mx2 = qz_absmax2(mx2, u.x, bf16);
-                    mx2 = qz_absmax2(mx2, u.y, bf16);
-                    mx2 = qz_absmax2(mx2, u.z, bf16);
-                    mx2 = qz_absmax2(mx2, u.w, bf16);
-                } else {
-                    for (int j = 0; j < 8 && k0 + j < K; ++j) mx2 = qz_absmax2(mx2, hrow[k0 + j], bf16);
+            for (int64_t base = (int64_t)lane * 8; base < K; base += 1024) {
+                uint4 u[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) u[t] = qz_load_half8(hrow, base + t * 256, K, vec);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    mx2 = qz_absmax2(mx2, u[t].x, bf16);
+                    mx2 = qz_absmax2(mx2, u[t].y, bf16);
+                    mx2 = qz_absmax2(mx2, u[t].z, bf16);
+                    mx2 = qz_absmax2(mx2, u[t].w, bf16);
+                    keep[t] = u[t];
                 }
             }
             const float a0 = qz_half_to_f32(mx2 & 0xFFFFu, bf16), a1 = qz_half_to_f32(mx2 >> 16, bf16);
@@ -211,64 +319,35 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __grid_constan
         const bool markstein = finite && half;
         const float y = __frcp_rn(s);
 
-        // ---- pass 2: e4m3 codes, codebook values, digit planes ----
-        const int64_t kq = P.planes ? ldp : K;   // planes are zero-filled up to ldp
-        for (int64_t k0 = (int64_t)lane * 8; k0 < kq; k0 += 256) {
-            float v[8];
-            load8(row, dtype, k0, K, vec, v);
-            uint32_t qw[2];
-            if (finite) {
-                float qv[8];
+        // ---- pass 2: codes, codebook values, digit planes (planes zero-filled to ldp) ----
+        QzRow R;
+        R.q = P.q + m * P.ldq;
+        R.cb = P.codebook ? P.codebook + m * P.ldc : nullptr;
+        R.pl = P.planes ? P.planes + m * P.ldp : nullptr;
+        R.pstride = P.M * P.ldp;
+        R.K = K;
+        R.qvec = qvec;
+        const int64_t kq = P.planes ? P.ldp : K;
+        if (markstein) {   // finite scale, half-precision input: the fast path
+            for (int64_t base = (int64_t)lane * 8; base < kq; base += 1024) {
+                uint4 u[4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) qv[j] = markstein ? qz_div(v[j], s, y) : __fdiv_rn(v[j], s);
-                qw[0] = qz_cvt_e4m3x2(qv[0], qv[1]) | (qz_cvt_e4m3x2(qv[2], qv[3]) << 16);
-                qw[1] = qz_cvt_e4m3x2(qv[4], qv[5]) | (qz_cvt_e4m3x2(qv[6], qv[7]) << 16);
-                if (k0 + 8 > K) {   // ragged tail: codes beyond K are zero
+                for (int t = 0; t < 4; ++t) u[t] = resident ? keep[t] : qz_load_half8(hrow, base + t * 256, K, vec);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (k0 + j >= K) qw[j >> 2] &= ~(0xFFu << (8 * (j & 3)));
-                }
-            } else {
-                qw[0] = qw[1] = 0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    uint32_t b = (k0 + j < K) ? ima_f32_to_e4m3(__fdiv_rn(v[j], s)) : 0u;
-                    qw[j >> 2] |= b << (8 * (j & 3));
+                for (int t = 0; t < 4; ++t) {
+                    const int64_t k0 = base + t * 256;
+                    if (k0 >= kq) break;
+                    float v[8];
+                    qz_unpack_half8(u[t], bf16, v);
+                    qz_emit(R, k0, qz_codes_fast(v, s, y), s_lut, s_code);
                 }
             }
-            int32_t cv[8];
-            uint32_t pw[3][2] = {{0, 0}, {0, 0}, {0, 0}};
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint32_t b = (qw[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-                const int32_t c = finite ? qz_codebook(b) : ima_e4m3_codebook(b);
-                cv[j] = c;
-                // balanced base-128 digits: u = c + 64 + 64 * 128 has digits (d0+64, d1+64, d2)
-                const int32_t u = c + 8256;
-                const uint32_t d0 = (uint32_t)((u & 127) - 64), d1 = (uint32_t)(((u >> 7) & 127) - 64);
-                const uint32_t d2 = (uint32_t)(u >> 14);
-                pw[0][j >> 2] |= (d0 & 0xFFu) << (8 * (j & 3));
-                pw[1][j >> 2] |= (d1 & 0xFFu) << (8 * (j & 3));
-                pw[2][j >> 2] |= (d2 & 0xFFu) << (8 * (j & 3));
-            }
-            if (k0 < K) {
-                if (qvec && k0 + 8 <= K) {
-                    *reinterpret_cast<uint2*>(qrow + k0) = make_uint2(qw[0], qw[1]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (k0 + j < K) qrow[k0 + j] = (uint8_t)(qw[j >> 2] >> (8 * (j & 3)));
-                }
-                if (P.codebook) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (k0 + j < K) P.codebook[m * ldc + k0 + j] = cv[j];
-                }
-            }
-            if (P.planes) {
-#pragma unroll
-                for (int i = 0; i < 3; ++i)
-                    *reinterpret_cast<uint2*>(P.planes + ((int64_t)i * M + m) * ldp + k0) = make_uint2(pw[i][0], pw[i][1]);
+        } else {           // fp32 input, or a NaN / infinite scale: IEEE division per element
+#pragma unroll 1
+            for (int64_t k0 = (int64_t)lane * 8; k0 < kq; k0 += 256) {
+                float v[8];
+                load8(row, dtype, k0, K, vec, v);
+                qz_emit(R, k0, qz_codes_ieee(v, s, finite, K - k0), s_lut, s_code);
             }
         }
     }
