@@ -25,10 +25,10 @@
 //   warp 0    TMA producer (no cluster multicast anywhere);
 //   warp 1    TMEM allocator and single-thread MMA issuer (2 x NP^2 MMAs of K = 32 per stage);
 //   warps 2-9 epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (one output row per
-//             thread) and half of the tile's columns, recombines int64, applies the fused
+//             thread) and half of the tile's columns, recombines them into int64 registers and
+//             hands the accumulators back to the MMA warp at once; it then applies the fused
 //             rescale, stages 32 x CHUNK chunks in swizzled shared memory and copies them out
-//             with coalesced 16-byte stores.  The accumulators are handed back to the MMA
-//             warp as soon as the last chunk is read.
+//             with coalesced 16-byte stores while the next tile's MMAs run.
 // Every mbarrier wait is bounded (IMA_WAIT_LIMIT_NS); a timeout records
 // IMA_ERR_TIMEOUT in the device status word and the CTA drains and exits.
 #include <cudaTypedefs.h>
@@ -260,12 +260,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
             const int64_t m = (int64_t)m0 + q * 32 + lane;
             const bool row_ok = m < P.M;
             const float xs = (row_ok && P.y) ? P.xs[m] : 0.0f;
-#pragma unroll 1
-            for (int c0 = 0; c0 < HALF; c0 += CHUNK) {
-                uint64_t cval[CHUNK];
+            // Drain: every accumulator column of this warp into int64 registers, then hand
+            // TMEM back at once, so that the conversion and copy-out below overlap the MMAs
+            // of the next tile.
+            uint64_t call[HALF];
 #pragma unroll
-                for (int j = 0; j < CHUNK; ++j) cval[j] = 0;
-                if (P.k_tiles > 0) {
+            for (int j = 0; j < HALF; ++j) call[j] = 0;
+            if (P.k_tiles > 0) {
+#pragma unroll
+                for (int c0 = 0; c0 < HALF; c0 += CHUNK) {
                     uint32_t r[NACC][CHUNK];
 #pragma unroll
                     for (int a = 0; a < NACC; ++a) {
@@ -278,14 +281,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                     for (int a = 0; a < NACC; ++a) {
 #pragma unroll
                         for (int j = 0; j < CHUNK; ++j)
-                            cval[j] += (uint64_t)(int64_t)(int32_t)r[a][j] << (7 * a);
+                            call[c0 + j] += (uint64_t)(int64_t)(int32_t)r[a][j] << (7 * a);
                     }
                 }
-                if (c0 + CHUNK >= HALF) {
-                    // every accumulator column of this warp has been read: release TMEM
-                    tc_fence_before();
-                    mbar_arrive(tmem_empty);
-                }
+            }
+            tc_fence_before();
+            mbar_arrive(tmem_empty);
+#pragma unroll
+            for (int c0 = 0; c0 < HALF; c0 += CHUNK) {
+                const uint64_t* cval = call + c0;
                 float yv[CHUNK];
 #pragma unroll
                 for (int j = 0; j < CHUNK; ++j) {
