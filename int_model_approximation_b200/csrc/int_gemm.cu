@@ -13,8 +13,16 @@
 // C is formed modulo 2^64, i.e. exactly the reference's wrapping int64 accumulator.
 //
 // Data movement.  A stage holds one 64-byte K-slice of all NP A planes (128 rows each) and
-// all NP B planes (BN rows each), 64-byte swizzled; each operand byte crosses L2 -> SM once
-// per tile and feeds NP MMAs.
+// all NP B planes (BN rows each, stacked), 64-byte swizzled; each operand byte crosses
+// L2 -> SM once per tile.
+//
+// MMA fan-out.  The accumulators c_0 .. c_{2NP-2} sit side by side in tensor memory, BN
+// columns each, so A_i times the stacked B planes [B_0; ..; B_{NP-1}] (one MMA of
+// N = NP * BN <= 256) lands A_i B_j^T in accumulator i + j for every j at once: NP MMAs per
+// 32-byte K step instead of NP^2, and each A plane is read from shared memory once.  The
+// MMA of i = 0 in the first K step of a tile overwrites accumulators 0 .. NP-1; the others
+// accumulate, so accumulators NP .. 2NP-2 must start at zero: the epilogue warps zero them
+// with tcgen05.st after draining a tile (and once at kernel start).
 //
 // One launch processes a batch of up to GM_MAXP independent problems (e.g. every linear
 // of a model): the problem descriptors and their TMA tensor maps travel in the kernel
@@ -51,9 +59,9 @@ struct Scheme;
 template <>
 struct Scheme<IMA_SCHEME_DIGITS3> {
     static constexpr int NP = 3;
-    static constexpr int BN = 96;
+    static constexpr int BN = 80;          // NP * BN = 240 <= 256 (one MMA per A plane)
     static constexpr int STAGES = 4;
-    static constexpr int CHUNK = 16;       // epilogue columns per tcgen05.ld
+    static constexpr int CHUNK = 8;        // epilogue columns per tcgen05.ld
 };
 
 template <>
@@ -76,6 +84,8 @@ struct GemmCfg {
     static constexpr int HALF = BN / 2;                     // columns per epilogue warp
     static_assert(HALF % CHUNK == 0, "columns per epilogue warp must be whole chunks");
     static_assert(NACC * BN <= (int)GM_TMEM_COLS, "accumulators exceed tensor memory");
+    static_assert(NP * BN <= 256 && (NP * BN) % 16 == 0, "stacked B planes must form one MMA of N <= 256");
+    static_assert((BN * GM_KT) % 512 == 0, "each stacked B plane must start on a 64-byte swizzle atom");
     static constexpr int A_PLANE = GM_BM * GM_KT;           // 8 KB
     static constexpr int B_PLANE = BN * GM_KT;
     static constexpr int STAGE_BYTES = NP * (A_PLANE + B_PLANE);
@@ -193,12 +203,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
         }
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer ----------------
-        constexpr uint32_t idesc = idesc_i8(GM_BM, BN);
+        constexpr uint32_t idesc = idesc_i8(GM_BM, NP * BN);
         uint32_t stage = 0, phase = 0, tphase = 0;
         for (int64_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
             const GemmProblemDev& P = batch.p[find_problem(batch, t)];
-            // wait until the epilogue drained the accumulators of the previous tile
-            if (!mbar_wait_bounded(tmem_empty, tphase ^ 1u, IMA_WHERE_GEMM_MMA, -1)) { *abort_flag = 1; break; }
+            // wait until the epilogue drained the previous tile and zeroed accumulators
+            // NP .. NACC-1 (for the first tile: zeroed them at kernel start)
+            if (!mbar_wait_bounded(tmem_empty, tphase, IMA_WHERE_GEMM_MMA, -1)) { *abort_flag = 1; break; }
             tphase ^= 1u;
             tc_fence_after();
             for (int kt = 0; kt < P.k_tiles; ++kt) {
@@ -213,17 +224,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                 for (int ks = 0; ks < GM_KT / 32; ++ks) {
 #pragma unroll
                     for (int i = 0; i < NP; ++i) {
-#pragma unroll
-                        for (int j = 0; j < NP; ++j) {
-                            // the first product into accumulator s = i + j of a tile overwrites it:
-                            // in this (i outer, j inner) order that is (0, s) for s < NP and
-                            // (s - NP + 1, NP - 1) otherwise
-                            const bool first = kt == 0 && ks == 0 && (i == 0 || j == NP - 1);
-                            mma_i8(tmem_base + (uint32_t)((i + j) * BN),
-                                   umma_desc_sw64_kmajor(sa + i * L::A_PLANE + ks * 32),
-                                   umma_desc_sw64_kmajor(sb + j * L::B_PLANE + ks * 32), idesc,
-                                   first ? 0u : 1u);
-                        }
+                        // accumulators i .. i+NP-1 += A_i [B_0; ..; B_{NP-1}]^T
+                        const bool first = kt == 0 && ks == 0 && i == 0;
+                        mma_i8(tmem_base + (uint32_t)(i * BN), umma_desc_sw64_kmajor(sa + i * L::A_PLANE + ks * 32),
+                               umma_desc_sw64_kmajor(sb + ks * 32), idesc, first ? 0u : 1u);
                     }
                 }
                 mma_commit(&empty[stage]);
@@ -237,6 +241,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
         const int q = warp & 3;                // TMEM lane quadrant of this warp
         const int h = ew >> 2;                 // column half of the tile
         uint32_t tphase = 0, tile_ctr = 0;
+        // zero this warp's share of accumulators NP .. NACC-1, then hand TMEM to the MMA warp
+        auto zero_upper_and_release = [&]() {
+            const uint32_t zero[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+            for (int a = NP; a < NACC; ++a)
+#pragma unroll
+                for (int c0 = 0; c0 < HALF; c0 += 8)
+                    tmem_st8(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN + h * HALF + c0), zero);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(tmem_empty);
+        };
+        zero_upper_and_release();
         for (int64_t t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_ctr) {
             const int pi = find_problem(batch, t);
             const GemmProblemDev& P = batch.p[pi];
@@ -285,8 +302,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                     }
                 }
             }
-            tc_fence_before();
-            mbar_arrive(tmem_empty);
+            zero_upper_and_release();
 #pragma unroll
             for (int c0 = 0; c0 < HALF; c0 += CHUNK) {
                 const uint64_t* cval = call + c0;
