@@ -15,6 +15,15 @@ materialising any counts.  The class bookkeeping that defines the checkable prod
 torch.unique sync per group) yields the same product count and class maxima as the
 reference; each checkable product bumps the active int32 probe once, exactly as the
 reference's raw_matmul calls do.
+
+A caller that injects its own raw_matmul (and does not ask for fused_replay) gets the
+reference's materialised products: the same one-hot / lane-packed operands in the same
+order, one call per checkable product.  Each returned product is Freivalds-checked on the
+GPU against its operands (a wrong product raises), and the output, a function of the
+counts, is then produced by the direct replay, bit-identical to replaying the counts.
+The count-product helpers keep the reference's names and layouts
+(hawkeye_freivalds.py:39-57, :147-213, :593-704, :840-841), so code written against them
+runs unchanged.
 """
 
 from __future__ import annotations
@@ -52,6 +61,160 @@ class HawkeyeFreivaldsStats:
 
 
 RawIntMatmul = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+# ---------------------------------------------------------------------------
+# Class ids and count-product operands (the reference's layouts; any device)
+# ---------------------------------------------------------------------------
+def _decode_fp8_fields(x_fp8: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(effective exponent, signed 4-bit significand, present) of every e4m3 element, int64.
+    ref: hawkeye_freivalds.py:39-48."""
+    b = x_fp8.contiguous().view(torch.uint8).to(torch.int64)
+    field = (b >> 3) & 0xF
+    mag = torch.where(field != 0, (b & 7) | 8, b & 7)
+    exp = torch.clamp(field, min=1)
+    sig = torch.where((b & 0x80) != 0, -mag, mag)
+    return exp, sig, mag != 0
+
+
+def _class_ids(exp_eff: torch.Tensor, signed_sig: torch.Tensor, nonzero: torch.Tensor) -> torch.Tensor:
+    """class = (e - 1) * 31 + (s + 15) for present elements, -1 otherwise.  ref: :51-57."""
+    ids = (exp_eff - 1) * SIGNED_SIG_BUCKETS + signed_sig + SIGNED_SIG_OFFSET
+    return ids.masked_fill(~nonzero, -1)
+
+
+def _iter_class_chunks(classes: torch.Tensor, chunk_size: int) -> list[torch.Tensor]:
+    """Consecutive slices of at most chunk_size classes.  ref: :840-841."""
+    return [classes[i:i + chunk_size] for i in range(0, int(classes.numel()), chunk_size)]
+
+
+def _one_hot_rows(class_group: torch.Tensor, classes: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """[len(classes) * rows, k]: row (c, r) marks the k where class_group[r, k] == classes[c]."""
+    rows, k = class_group.shape
+    hit = class_group.unsqueeze(0) == classes.reshape(-1, 1, 1)
+    return hit.to(dtype).reshape(int(classes.numel()) * rows, k).contiguous()
+
+
+def _weight_chunk_flat(
+    b_class_group: torch.Tensor, b_classes: torch.Tensor, *, count_dtype: torch.dtype = torch.int32
+) -> torch.Tensor:
+    """[k, len(b_classes) * N]: column (c, n) marks the k where b_class_group[n, k] == b_classes[c].
+    ref: :188-199."""
+    return _one_hot_rows(b_class_group, b_classes, count_dtype).t().contiguous()
+
+
+def _class_chunk_product_raw_with_b_flat(
+    a_class_group: torch.Tensor, a_classes: torch.Tensor, b_flat: torch.Tensor, b_size: int, raw_matmul: RawIntMatmul
+) -> tuple[torch.Tensor, int, int]:
+    """raw_matmul(one-hot A, b_flat) -> ([a_size * M, b_size * N], a_size, b_size).  ref: :202-213."""
+    a_flat = _one_hot_rows(a_class_group, a_classes, b_flat.dtype)
+    return raw_matmul(a_flat, b_flat), int(a_classes.numel()), b_size
+
+
+def _class_chunk_product_raw(
+    a_class_group: torch.Tensor,
+    b_class_group: torch.Tensor,
+    a_classes: torch.Tensor,
+    b_classes: torch.Tensor,
+    raw_matmul: RawIntMatmul,
+    *,
+    count_dtype: torch.dtype = torch.int32,
+) -> tuple[torch.Tensor, int, int]:
+    """The unpacked count product, flat.  ref: :166-185."""
+    b_flat = _weight_chunk_flat(b_class_group, b_classes, count_dtype=count_dtype)
+    return _class_chunk_product_raw_with_b_flat(a_class_group, a_classes, b_flat, int(b_classes.numel()), raw_matmul)
+
+
+def _class_chunk_product(
+    a_class_group: torch.Tensor,
+    b_class_group: torch.Tensor,
+    a_classes: torch.Tensor,
+    b_classes: torch.Tensor,
+    raw_matmul: RawIntMatmul,
+    *,
+    count_dtype: torch.dtype = torch.int32,
+) -> torch.Tensor:
+    """counts[a, b, m, n] = #k with class a at (m, k) and class b at (n, k).  ref: :147-163."""
+    flat, a_size, b_size = _class_chunk_product_raw(
+        a_class_group, b_class_group, a_classes, b_classes, raw_matmul, count_dtype=count_dtype
+    )
+    m, n = a_class_group.shape[0], b_class_group.shape[0]
+    return flat.reshape(a_size, m, b_size, n).permute(0, 2, 1, 3)
+
+
+def _lane_packed_classes(b_classes: torch.Tensor, lanes: int) -> torch.Tensor:
+    """b_classes laid out [ceil(nb / lanes), lanes], unused lanes -2 (never a class)."""
+    groups = -(-int(b_classes.numel()) // lanes)
+    out = torch.full((groups, lanes), -2, dtype=b_classes.dtype, device=b_classes.device)
+    out.view(-1)[: b_classes.numel()] = b_classes
+    return out
+
+
+def _lane_packed_b_flat(
+    b_class_pack: torch.Tensor, packed: torch.Tensor, lane_of_k: torch.Tensor, lanes_per_group: int
+) -> torch.Tensor:
+    """[k, groups * N] int32: 64^lane summed over the lane whose class matches (n, k); the lane of
+    class slot j at k is lane_of_k[k] * lanes_per_group + j."""
+    groups, slots = packed.shape
+    n, k = b_class_pack.shape
+    hit = b_class_pack.unsqueeze(0).unsqueeze(0) == packed.reshape(groups, slots, 1, 1)   # [G, S, N, K]
+    lane = lane_of_k.reshape(1, 1, 1, k) * lanes_per_group + torch.arange(slots, device=packed.device).reshape(1, slots, 1, 1)
+    weight = torch.bitwise_left_shift(torch.ones_like(lane), PACKED_COUNT_BASE_LOG2 * lane)
+    value = (hit.to(torch.int64) * weight).sum(dim=1)                                      # [G, N, K]
+    return value.permute(2, 0, 1).reshape(k, groups * n).to(torch.int32).contiguous()
+
+
+def _packed_class_chunk_product(
+    a_class_group: torch.Tensor,
+    b_class_group: torch.Tensor,
+    a_classes: torch.Tensor,
+    b_classes: torch.Tensor,
+    raw_matmul: RawIntMatmul,
+    packed_count_lanes: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Counts of up to packed_count_lanes weight classes per int64, base 64.
+    Returns (counts [a, packed group, m, n], packed_b_classes [groups, lanes]).  ref: :593-631."""
+    packed = _lane_packed_classes(b_classes, packed_count_lanes)
+    k = a_class_group.shape[1]
+    b_flat = _lane_packed_b_flat(b_class_group, packed, torch.zeros(k, dtype=torch.int64, device=packed.device),
+                                 packed_count_lanes)
+    a_flat = _one_hot_rows(a_class_group, a_classes, torch.int32)
+    flat = raw_matmul(a_flat, b_flat)
+    m, n = a_class_group.shape[0], b_class_group.shape[0]
+    return flat.reshape(int(a_classes.numel()), m, packed.shape[0], n).permute(0, 2, 1, 3), packed
+
+
+def _packed_group_class_chunk_product(
+    a_class_pack: torch.Tensor,
+    b_class_pack: torch.Tensor,
+    a_classes: torch.Tensor,
+    b_classes: torch.Tensor,
+    raw_matmul: RawIntMatmul,
+    *,
+    products_per_group: int,
+    packed_group_lanes: int,
+    packed_count_lanes: int,
+) -> tuple[torch.Tensor, torch.Tensor, int]:
+    """Counts of a pack of groups: lane = group * (lanes // group lanes) + weight-class slot.
+    Returns (counts [a, packed group, m, n], packed_b_classes, weight lanes per group).  ref: :634-704."""
+    k = a_class_pack.shape[1]
+    groups_in_pack = -(-k // products_per_group)
+    if groups_in_pack > packed_group_lanes:
+        raise RuntimeError("group pack contains more groups than packed_group_lanes")
+    if packed_group_lanes < 1 or packed_group_lanes > packed_count_lanes:
+        raise ValueError("packed_group_lanes must fit inside packed_count_lanes")
+    b_lanes = packed_count_lanes // packed_group_lanes
+    if b_lanes < 1:
+        raise ValueError("packed_group_lanes leaves no lanes for weight classes")
+    if packed_group_lanes * b_lanes > MAX_PACKED_COUNT_LANES:
+        raise ValueError("too many packed count lanes")
+    packed = _lane_packed_classes(b_classes, b_lanes)
+    lane_of_k = torch.arange(k, device=packed.device) // products_per_group
+    b_flat = _lane_packed_b_flat(b_class_pack, packed, lane_of_k, b_lanes)
+    a_flat = _one_hot_rows(a_class_pack, a_classes, torch.int32)
+    flat = raw_matmul(a_flat, b_flat)
+    m, n = a_class_pack.shape[0], b_class_pack.shape[0]
+    return flat.reshape(int(a_classes.numel()), m, packed.shape[0], n).permute(0, 2, 1, 3), packed, b_lanes
 
 
 def class_presence(fp8: torch.Tensor, pack_width: int) -> torch.Tensor:
@@ -125,6 +288,94 @@ def class_count_stats(
     )
 
 
+class _CheckedMatmul:
+    """Wraps an injected raw_matmul: every product it returns is Freivalds-checked on the GPU
+    against its operands before use, and calls are counted."""
+
+    def __init__(self, inner: RawIntMatmul):
+        self.inner = inner
+        self.calls = 0
+
+    def __call__(self, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+        from .freivalds import freivalds_vector, mismatch_rows_int32
+
+        c = self.inner(a, b)
+        self.calls += 1
+        m, n = int(a.shape[0]), int(b.shape[1])
+        if not isinstance(c, torch.Tensor) or tuple(c.shape) != (m, n) or c.dtype not in (torch.int32, torch.int64):
+            raise RuntimeError(
+                f"raw_matmul returned {getattr(c, 'dtype', type(c))} {tuple(getattr(c, 'shape', ()))} "
+                f"for a ({m}, {int(a.shape[1])}) x ({int(b.shape[0])}, {n}) integer count product"
+            )
+        dev = c.device
+        r = freivalds_vector(n, 0x5EED + self.calls, device=dev)
+        bad = mismatch_rows_int32(a.to(device=dev, dtype=torch.int32), b.to(device=dev, dtype=torch.int32),
+                                  c.to(torch.int64), r)
+        if int(bad.item()) != 0:
+            raise RuntimeError(
+                f"raw_matmul returned a class-count product ({m} x {n}) that fails the Freivalds check "
+                f"on {int(bad.item())} rows"
+            )
+        return c
+
+
+def _materialise_count_products(
+    x_fp8: torch.Tensor,
+    w_fp8: torch.Tensor,
+    raw_matmul: RawIntMatmul,
+    *,
+    products_per_group: int,
+    class_chunk: int,
+    packed_count_lanes: int,
+    packed_group_lanes: int,
+    fused_replay: bool,
+    cache_weight_chunks: bool,
+    count_dtype: torch.dtype,
+) -> int:
+    """Form every checkable count product the way the reference does (same operands, same
+    order: hawkeye_freivalds.py:900-932 for packed groups, :1086-1207 otherwise), each
+    through a Freivalds-checked call of raw_matmul.  Returns the number of calls."""
+    checked = _CheckedMatmul(raw_matmul)
+    a_class = _class_ids(*_decode_fp8_fields(x_fp8))
+    b_class = _class_ids(*_decode_fp8_fields(w_fp8))
+    k_size = a_class.shape[1]
+    if packed_group_lanes > 1:
+        width = products_per_group * packed_group_lanes
+        b_lanes = packed_count_lanes // packed_group_lanes
+        for k0 in range(0, k_size, width):
+            a_pack, b_pack = a_class[:, k0:k0 + width], b_class[:, k0:k0 + width]
+            a_classes = torch.unique(a_pack[a_pack >= 0])
+            b_classes = torch.unique(b_pack[b_pack >= 0])
+            for a_chunk in _iter_class_chunks(a_classes, class_chunk):
+                for b_chunk in _iter_class_chunks(b_classes, class_chunk * b_lanes):
+                    _packed_group_class_chunk_product(
+                        a_pack, b_pack, a_chunk, b_chunk, checked, products_per_group=products_per_group,
+                        packed_group_lanes=packed_group_lanes, packed_count_lanes=packed_count_lanes,
+                    )
+        return checked.calls
+    for k0 in range(0, k_size, products_per_group):
+        a_group, b_group = a_class[:, k0:k0 + products_per_group], b_class[:, k0:k0 + products_per_group]
+        a_classes = torch.unique(a_group[a_group >= 0])
+        b_classes = torch.unique(b_group[b_group >= 0])
+        b_chunk_size = class_chunk if packed_count_lanes == 1 else class_chunk * packed_count_lanes
+        b_chunks = _iter_class_chunks(b_classes, b_chunk_size)
+        cached = None
+        if cache_weight_chunks and packed_count_lanes == 1 and not fused_replay:
+            cached = [(int(c.numel()), _weight_chunk_flat(b_group, c, count_dtype=count_dtype)) for c in b_chunks]
+        for a_chunk in _iter_class_chunks(a_classes, class_chunk):
+            if cached is not None:
+                for b_size, b_flat in cached:
+                    _class_chunk_product_raw_with_b_flat(a_group, a_chunk, b_flat, b_size, checked)
+                continue
+            for b_chunk in b_chunks:
+                if packed_count_lanes == 1:
+                    if not fused_replay:   # the fused reference kernel forms these counts itself
+                        _class_chunk_product(a_group, b_group, a_chunk, b_chunk, checked, count_dtype=count_dtype)
+                else:
+                    _packed_class_chunk_product(a_group, b_group, a_chunk, b_chunk, checked, packed_count_lanes)
+    return checked.calls
+
+
 def _bump_probe(count: int) -> None:
     # The reference bumps __main__._ACTIVE_INT32_PROBE once per raw_matmul launch
     # (__main__.py:239-240); the students module owns the probe here.
@@ -154,10 +405,13 @@ def exact_hawkeye_fp8_sum(
 ) -> tuple[torch.Tensor, HawkeyeFreivaldsStats]:
     """Replay Hawkeye exactly from Freivalds-checkable class-count products.
 
-    ref: hawkeye_freivalds.py:1017-1246.  `raw_matmul` is accepted for signature
-    compatibility: the B200 engine forms the count products itself (fused), so the
-    callable is not invoked; every checkable product is still counted on the active
-    int32 probe.
+    ref: hawkeye_freivalds.py:1017-1246.  With raw_matmul None or this package's own
+    _int32_raw_matmul (what HawkeyeClassCountsLinear passes, as the reference does) the
+    counts are folded into the replay engine and never materialised; the active int32 probe
+    is bumped once per product the reference would have sent through _int32_raw_matmul.
+    Any other raw_matmul receives the reference's products, one call each, and every result
+    is Freivalds-checked (RuntimeError if one fails).  The output is the direct replay in
+    both cases.
     """
     if count_dtype not in {torch.int8, torch.int32}:
         raise ValueError(f"count_dtype must be torch.int8 or torch.int32, got {count_dtype}")
@@ -214,7 +468,19 @@ def exact_hawkeye_fp8_sum(
         packed_count_lanes=packed_count_lanes,
         packed_group_lanes=packed_group_lanes,
     )
-    _bump_probe(stats.total_checkable_products)
+    reference_calls = 0 if (fused_replay and packed_count_lanes == 1) else stats.total_checkable_products
+    from . import students
+
+    if raw_matmul is None or raw_matmul is students._int32_raw_matmul:
+        _bump_probe(reference_calls)
+    else:
+        made = _materialise_count_products(
+            x_fp8, w_fp8, raw_matmul, products_per_group=products_per_group, class_chunk=class_chunk,
+            packed_count_lanes=packed_count_lanes, packed_group_lanes=packed_group_lanes,
+            fused_replay=fused_replay, cache_weight_chunks=cache_weight_chunks, count_dtype=count_dtype,
+        )
+        if made != reference_calls:
+            raise RuntimeError(f"internal: {made} count products formed, {reference_calls} expected")
 
     x_op = HawkeyeOperand(x_fp8)
     w_op = stage_weight(w_fp8)

@@ -328,6 +328,66 @@ def test_class_counts_c3_shape_against_direct_and_oracle(cuda_device):
     assert stats.groups == 152
 
 
+def _small_class_count_case(device):
+    x = synthetic.student_t_activations(24, 200, seed=21, outlier_fraction=0.02)
+    xq, xs = oracle.per_token_fp8(x)
+    w, ws = synthetic.normal_fp8_weights(40, 200, seed=22)
+    return xq.to(device), xs.to(device), w.to(device), ws.to(device)
+
+
+@pytest.mark.parametrize(
+    "params",
+    [
+        dict(class_chunk=32),
+        dict(class_chunk=8, packed_count_lanes=6),
+        dict(class_chunk=16, packed_count_lanes=6, packed_group_lanes=2),
+        dict(class_chunk=32, cache_weight_chunks=True),
+        dict(class_chunk=8, count_dtype=torch.int8),
+    ],
+)
+def test_class_counts_with_an_injected_raw_matmul(cuda_device, params):
+    """An injected raw_matmul receives the reference's count products, one call per
+    checkable product, each Freivalds-checked; the output equals the fused engine's and the
+    oracle's bit for bit."""
+    xq, xs, w, ws = _small_class_count_case(cuda_device)
+    shapes = []
+
+    def logging_matmul(a, b):
+        shapes.append((tuple(a.shape), tuple(b.shape)))
+        return students._int32_raw_matmul(a.to(torch.int32), b.to(torch.int32))
+
+    y, stats = hawkeye_freivalds.exact_hawkeye_fp8_sum(xq, xs, w, ws, logging_matmul, **params)
+    fused, fused_stats = hawkeye_freivalds.exact_hawkeye_fp8_sum(xq, xs, w, ws, students._int32_raw_matmul, **params)
+    assert len(shapes) == stats.total_checkable_products == fused_stats.total_checkable_products > 0
+    assert all(a[1] == b[0] and a[0] % 24 == 0 and b[1] % 40 == 0 for a, b in shapes)
+    assert torch.equal(y.view(torch.int16), fused.view(torch.int16))
+    ref = oracle.hawkeye(xq.cpu(), xs.cpu(), w.cpu(), ws.cpu()).to(torch.bfloat16)
+    assert torch.equal(y.cpu().view(torch.int16), ref.view(torch.int16))
+
+
+def test_class_counts_reject_a_wrong_injected_product(cuda_device):
+    xq, xs, w, ws = _small_class_count_case(cuda_device)
+
+    def tampered(a, b):
+        c = students._int32_raw_matmul(a, b)
+        c[3, 1] += 1
+        return c
+
+    with pytest.raises(RuntimeError, match="fails the Freivalds check"):
+        hawkeye_freivalds.exact_hawkeye_fp8_sum(xq, xs, w, ws, tampered)
+
+
+def test_class_count_probe_counts_only_products_the_reference_sends_through_raw_matmul(cuda_device):
+    xq, xs, w, ws = _small_class_count_case(cuda_device)
+    with students._Int32KernelProbe() as probe:
+        _, stats = hawkeye_freivalds.exact_hawkeye_fp8_sum(xq, xs, w, ws, students._int32_raw_matmul)
+    assert probe.count == stats.total_checkable_products > 0
+    with students._Int32KernelProbe() as probe:
+        _, stats = hawkeye_freivalds.exact_hawkeye_fp8_sum(xq, xs, w, ws, students._int32_raw_matmul,
+                                                           fused_replay=True)
+    assert probe.count == 0 and stats.total_checkable_products > 0
+
+
 # ---------------------------------------------------------------------------
 # the plugin surface end to end
 # ---------------------------------------------------------------------------

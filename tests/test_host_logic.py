@@ -167,3 +167,95 @@ def test_class_count_stats_bookkeeping_matches_reference_loops(params):
         nb.append(int(torch.unique(b[b >= 0]).numel()))
     got = hawkeye_freivalds.class_count_stats(na, nb, 100, products_per_group=32, **params)
     assert got.__dict__ == expected
+
+
+# ---------------------------------------------------------------------------
+# Count-product helpers (reference layouts), on CPU with an int64 matmul
+# ---------------------------------------------------------------------------
+def _cpu_matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return a.to(torch.int64) @ b.to(torch.int64)
+
+
+def _brute_counts(a_cls, b_cls, a_classes, b_classes):
+    m, k = a_cls.shape
+    n = b_cls.shape[0]
+    out = torch.zeros((len(a_classes), len(b_classes), m, n), dtype=torch.int64)
+    for ai, a in enumerate(a_classes.tolist()):
+        for bi, b in enumerate(b_classes.tolist()):
+            out[ai, bi] = ((a_cls == a).to(torch.int64) @ (b_cls == b).to(torch.int64).t())
+    return out
+
+
+def test_class_ids_of_every_e4m3_byte_match_the_oracle():
+    codes = torch.arange(256, dtype=torch.int64).to(torch.uint8).view(torch.float8_e4m3fn).reshape(16, 16)
+    ids = hawkeye_freivalds._class_ids(*hawkeye_freivalds._decode_fp8_fields(codes))
+    assert torch.equal(ids, oracle.class_ids(codes))
+    assert int(ids.max()) < 15 * 31 and int((ids == -1).sum()) == 2   # +0 and -0
+
+
+def test_unpacked_class_count_product_counts_every_class_pair():
+    g = torch.Generator().manual_seed(5)
+    a_cls = torch.randint(-1, 6, (7, 32), generator=g)
+    b_cls = torch.randint(-1, 9, (5, 32), generator=g)
+    a_classes, b_classes = torch.tensor([0, 2, 3, 5]), torch.tensor([1, 4, 6, 7, 8])
+    counts = hawkeye_freivalds._class_chunk_product(a_cls, b_cls, a_classes, b_classes, _cpu_matmul)
+    assert torch.equal(counts.to(torch.int64), _brute_counts(a_cls, b_cls, a_classes, b_classes))
+
+
+@pytest.mark.parametrize("lanes", [2, 3, 6])
+def test_lane_packed_counts_decode_to_the_unpacked_counts(lanes):
+    g = torch.Generator().manual_seed(lanes)
+    a_cls = torch.randint(-1, 5, (6, 32), generator=g)
+    b_cls = torch.randint(-1, 11, (4, 32), generator=g)
+    a_classes, b_classes = torch.arange(5), torch.arange(11)
+    packed, packed_b = hawkeye_freivalds._packed_class_chunk_product(a_cls, b_cls, a_classes, b_classes,
+                                                                       _cpu_matmul, lanes)
+    assert packed_b.shape == ((11 + lanes - 1) // lanes, lanes)
+    want = _brute_counts(a_cls, b_cls, a_classes, b_classes)
+    for bi in range(11):
+        grp, lane = divmod(bi, lanes)
+        assert int(packed_b[grp, lane]) == bi
+        got = (packed[:, grp] >> (hawkeye_freivalds.PACKED_COUNT_BASE_LOG2 * lane)) & (hawkeye_freivalds.PACKED_COUNT_BASE - 1)
+        assert torch.equal(got, want[:, bi])
+    assert int((packed_b == -2).sum()) == packed_b.numel() - 11
+
+
+def test_group_packed_counts_decode_to_each_group():
+    g = torch.Generator().manual_seed(11)
+    ppg, group_lanes, lanes = 8, 2, 6
+    a_cls = torch.randint(-1, 4, (3, 2 * ppg), generator=g)
+    b_cls = torch.randint(-1, 5, (4, 2 * ppg), generator=g)
+    a_classes, b_classes = torch.arange(4), torch.arange(5)
+    packed, packed_b, b_lanes = hawkeye_freivalds._packed_group_class_chunk_product(
+        a_cls, b_cls, a_classes, b_classes, _cpu_matmul,
+        products_per_group=ppg, packed_group_lanes=group_lanes, packed_count_lanes=lanes,
+    )
+    assert b_lanes == lanes // group_lanes
+    for grp_lane in range(group_lanes):
+        sl = slice(grp_lane * ppg, (grp_lane + 1) * ppg)
+        want = _brute_counts(a_cls[:, sl], b_cls[:, sl], a_classes, b_classes)
+        for bi in range(5):
+            pg, slot = divmod(bi, b_lanes)
+            lane = grp_lane * b_lanes + slot
+            got = (packed[:, pg] >> (hawkeye_freivalds.PACKED_COUNT_BASE_LOG2 * lane)) & 63
+            assert torch.equal(got, want[:, bi])
+    with pytest.raises(RuntimeError, match="more groups than packed_group_lanes"):
+        hawkeye_freivalds._packed_group_class_chunk_product(
+            torch.zeros((1, 3 * ppg), dtype=torch.int64), torch.zeros((1, 3 * ppg), dtype=torch.int64),
+            a_classes, b_classes, _cpu_matmul, products_per_group=ppg, packed_group_lanes=2, packed_count_lanes=6)
+    with pytest.raises(ValueError, match="must fit inside packed_count_lanes"):
+        hawkeye_freivalds._packed_group_class_chunk_product(
+            a_cls, b_cls, a_classes, b_classes, _cpu_matmul, products_per_group=ppg, packed_group_lanes=7,
+            packed_count_lanes=6)
+
+
+def test_cached_weight_chunk_product_equals_the_plain_product():
+    g = torch.Generator().manual_seed(3)
+    a_cls = torch.randint(-1, 6, (5, 32), generator=g)
+    b_cls = torch.randint(-1, 6, (3, 32), generator=g)
+    a_classes, b_classes = torch.arange(6), torch.tensor([0, 1, 5])
+    b_flat = hawkeye_freivalds._weight_chunk_flat(b_cls, b_classes)
+    flat, a_size, b_size = hawkeye_freivalds._class_chunk_product_raw_with_b_flat(a_cls, a_classes, b_flat, 3,
+                                                                                  _cpu_matmul)
+    plain, _, _ = hawkeye_freivalds._class_chunk_product_raw(a_cls, b_cls, a_classes, b_classes, _cpu_matmul)
+    assert (a_size, b_size) == (6, 3) and torch.equal(flat, plain)
