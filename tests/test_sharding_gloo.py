@@ -112,3 +112,68 @@ def test_a_dead_rank_is_detected_by_the_survivor(tmp_path):
             p.kill()
     outcome = (tmp_path / "dying.txt").read_text()
     assert outcome.startswith("error"), outcome
+
+
+def _presence_masks(fp8: torch.Tensor, pack_width: int) -> torch.Tensor:
+    """CPU restatement of hawkeye_freivalds.class_presence: bit (c % 32) of word (c // 32)."""
+    import oracle
+
+    ids = oracle.class_ids(fp8)
+    k = ids.shape[1]
+    packs = max((k + pack_width - 1) // pack_width, 1)
+    masks = torch.zeros((packs, 16), dtype=torch.int64)
+    for p in range(packs):
+        for c in torch.unique(ids[:, p * pack_width:(p + 1) * pack_width]).tolist():
+            if c >= 0:
+                masks[p, c // 32] |= 1 << (c % 32)
+    return masks.to(torch.uint32).view(torch.int32) if hasattr(torch, "uint32") else masks.to(torch.int32)
+
+
+def _popcount_rows(masks: torch.Tensor) -> list[int]:
+    return [sum(bin(int(w) & 0xFFFFFFFF).count("1") for w in row) for row in masks.tolist()]
+
+
+def _class_worker(rank: int, world: int, port: int, result_dir: str) -> None:
+    import oracle
+    from int_model_approximation_b200 import hawkeye_freivalds as hf
+
+    try:
+        _init(rank, world, port)
+        x = synthetic.student_t_activations(29, 150, seed=4, outlier_fraction=0.05)
+        xq, _ = oracle.per_token_fp8(x)
+        w, _ = synthetic.normal_fp8_weights(9, 150, seed=5)
+        s, e = sharding.row_shard(29, world, rank)
+        width = 64   # 2 group lanes of 32
+        glob = sharding.global_class_presence(_presence_masks(xq[s:e], width), None)
+        full = _presence_masks(xq, width)
+        stats = hf.class_count_stats(_popcount_rows(glob), _popcount_rows(_presence_masks(w, width)), 150,
+                                     products_per_group=32, class_chunk=8, packed_count_lanes=6, packed_group_lanes=2)
+        ref = oracle.class_count_stats(xq, w, class_chunk=8, packed_count_lanes=6, packed_group_lanes=2)
+        # column-sharded Freivalds: partial vectors summed over ranks equal the unsharded ones
+        r = torch.randint(0, 1 << 20, (9,), generator=torch.Generator().manual_seed(6))
+        a = oracle.fp8_codebook(xq)
+        b = oracle.fp8_codebook(w)
+        c = oracle.int_gemm(a, b, b_is_nk=True)
+        cs, ce = sharding.row_shard(9, world, rank)
+        t_part = (b[cs:ce].t().to(torch.int64) @ r[cs:ce]).contiguous()
+        cr_part = (c[:, cs:ce] @ r[cs:ce]).contiguous()
+        sharding.combine_freivalds_partials(t_part)
+        sharding.combine_freivalds_partials(cr_part)
+        ok_check = torch.equal(a.to(torch.int64) @ t_part, cr_part)
+        if rank == 0:
+            with open(os.path.join(result_dir, "classes.txt"), "w") as f:
+                f.write(f"{int(torch.equal(glob, full))} {int(stats.__dict__ == ref)} {int(ok_check)}")
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:  # noqa: BLE001 - report to the parent
+        with open(os.path.join(result_dir, f"error{rank}.txt"), "w") as f:
+            f.write(traceback.format_exc())
+        raise
+
+
+def test_two_gloo_ranks_share_class_lists_and_freivalds_partials(tmp_path):
+    port = _free_port()
+    mp.start_processes(_class_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    errors = [p.read_text() for p in tmp_path.glob("error*.txt")]
+    assert not errors, errors
+    assert (tmp_path / "classes.txt").read_text().split() == ["1", "1", "1"]
