@@ -548,6 +548,176 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_c4(args) -> None:
+    """Config 4: the 196 FP8 linears of a Qwen2.5-7B-shaped model at `--c4-tokens` tokens
+    (16384), split over the ranks by token rows with the weights replicated, except
+    gate_proj/up_proj, whose weights are split by output columns (every rank then holds all
+    tokens for them).  Phase "codebook": per layer, the grouped quantiser, the exact int64
+    GEMM with the fused rescale and the Freivalds row check of every local product, then one
+    NCCL all-gather per linear of the bf16 output shards.  Phase "hawkeye": per linear,
+    quantise, stage and replay, then the same gathers.  Gathers run on a second stream and
+    overlap the next layer's compute (two output buffer sets alternate).  The seven
+    activation matrices of a layer are shared by all 28 layers (synthetic inputs of the
+    right shapes; the work per layer is unchanged), so memory stays within one GPU at N = 1.
+    Each phase is timed on the device (CUDA events, max over ranks)."""
+    import datetime
+
+    from int_model_approximation_b200 import _native as nat
+    from int_model_approximation_b200 import sharding, synthetic
+    from int_model_approximation_b200.codebook import DigitPlanes
+    from int_model_approximation_b200.hawkeye import HawkeyeOperand
+    from int_model_approximation_b200.pipeline import CodebookStack
+
+    world, rank, local = _dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = torch.distributed
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
+    lib = nat.lib()
+    tokens, layers = args.c4_tokens, args.c4_layers
+    phases = [p for p in args.c4_phases.split(",") if p]
+    if tokens % world:
+        raise SystemExit("--c4-tokens must be a multiple of the number of GPUs")
+    specs = []
+    for p, s in enumerate(synthetic.qwen_layer_shapes(3584, 512, 18944)):
+        if s.name in ("gate_proj", "up_proj"):
+            c0, c1 = sharding.col_shard(s.n, world, rank)
+            if (c1 - c0) * world != s.n:
+                raise SystemExit(f"{s.name}: {s.n} columns do not split evenly over {world} GPUs")
+            specs.append(dict(name=s.name, k=s.k, n=c1 - c0, n_full=s.n, rows=tokens, col=True))
+        else:
+            r0, r1 = sharding.row_shard(tokens, world, rank)
+            specs.append(dict(name=s.name, k=s.k, n=s.n, n_full=s.n, rows=r1 - r0, col=False))
+    xs = [synthetic.student_t_activations(sp["rows"], sp["k"], synthetic.linear_seed(4, p) + 1_000_003 * rank,
+                                          device=device) for p, sp in enumerate(specs)]
+    stacks, hk_w, hk_ws = [], [], []
+    for layer in range(layers):
+        lw = []
+        for p, sp in enumerate(specs):
+            seed = synthetic.linear_seed(4, 7 * layer + p) + 500_000 + (7919 * rank if sp["col"] else 0)
+            lw.append(synthetic.normal_fp8_weights(sp["n"], sp["k"], seed, device=device) + (None,))
+        if "codebook" in phases:
+            stacks.append(CodebookStack(lw, seed=layer))
+        if "hawkeye" in phases:
+            hk_w.append([HawkeyeOperand(w) for w, _ws, _b in lw])
+            hk_ws.append([ws.reshape(-1).to(torch.float32).contiguous() for _w, ws, _b in lw])
+        del lw
+
+    mismatch = torch.zeros((1,), dtype=torch.int32, device=device)
+
+    def buffer_set():
+        b = dict(q=[], scale=[], code_scale=[], planes=[], c=[], y=[], mismatch=mismatch)
+        for sp in specs:
+            rows, k, n = sp["rows"], sp["k"], sp["n"]
+            b["q"].append(torch.empty((rows, k), dtype=torch.uint8, device=device))
+            b["scale"].append(torch.empty((rows,), dtype=torch.float32, device=device))
+            b["code_scale"].append(torch.empty((rows,), dtype=torch.float32, device=device))
+            b["planes"].append(DigitPlanes.empty(rows, k, nat.IMA_SCHEME_DIGITS3, device))
+            b["c"].append(torch.empty((rows, n), dtype=torch.int64, device=device) if "codebook" in phases else None)
+            b["y"].append(torch.empty((rows, n), dtype=torch.bfloat16, device=device))
+        return b
+
+    sets = [buffer_set(), buffer_set()]
+    views = [[dict(sets[s]) for s in range(2)] for _ in range(len(stacks))]   # own descriptor caches
+    gathered = [torch.empty((world * sp["rows"], sp["n"]), dtype=torch.bfloat16, device=device) for sp in specs]
+    hk_xop = [torch.empty((int(lib.ima_hawkeye_operand_bytes(sp["rows"], sp["k"])),), dtype=torch.uint8,
+                          device=device) for sp in specs] if "hawkeye" in phases else []
+    cs, ms = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    computed = [torch.cuda.Event(), torch.cuda.Event()]
+    drained = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def gather(s: int) -> None:
+        computed[s].record(cs)
+        if world > 1:
+            ms.wait_event(computed[s])
+            with torch.cuda.stream(ms):
+                for p in range(len(specs)):
+                    dist.all_gather_into_tensor(gathered[p], sets[s]["y"][p])
+            drained[s].record(ms)
+        else:
+            drained[s].record(cs)
+
+    def hawkeye_layer(layer: int, s: int) -> None:
+        sp_ = cs.cuda_stream
+        b = sets[s]
+        for p, sp in enumerate(specs):
+            rows, k, n = sp["rows"], sp["k"], sp["n"]
+            nat.check("q", lib.ima_quantize_per_token(xs[p].data_ptr(), nat.IMA_DTYPE_BF16, rows, k, k,
+                                                      b["q"][p].data_ptr(), k, b["scale"][p].data_ptr(), None, k,
+                                                      None, None, 16, sp_))
+            nat.check("p", lib.ima_hawkeye_prepare(b["q"][p].data_ptr(), rows, k, k, hk_xop[p].data_ptr(), sp_))
+            nat.check("r", lib.ima_hawkeye_replay(hk_xop[p].data_ptr(), hk_w[layer][p].buffer.data_ptr(),
+                                                  b["scale"][p].data_ptr(), hk_ws[layer][p].data_ptr(), rows, n, k,
+                                                  32, 14, -139, b["y"][p].data_ptr(), n, None, n, sp_))
+
+    def step(phase: str) -> None:
+        for layer in range(layers):
+            s = layer % 2
+            if layer >= 2:
+                cs.wait_event(drained[s])   # the gather of layer - 2 has read this buffer set
+            with torch.cuda.stream(cs):
+                if phase == "codebook":
+                    stacks[layer].forward(xs, views[layer][s])
+                else:
+                    hawkeye_layer(layer, s)
+            gather(s)
+        for s in range(2):
+            cs.wait_event(drained[s])
+
+    def timed(phase: str, steps: int, warmup: int) -> float:
+        for _ in range(warmup):
+            step(phase)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cs)
+        for _ in range(steps):
+            step(phase)
+        e1.record(cs)
+        torch.cuda.synchronize()
+        ms_ = e0.elapsed_time(e1) / steps
+        t = torch.tensor([ms_], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.barrier()
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    shapes_full = synthetic.qwen_layer_shapes(3584, 512, 18944)
+    gather_bytes = sum(2 * (world - 1) * sp["rows"] * sp["n"] for sp in specs) * layers if world > 1 else 0
+    res = {"workload": f"c4: {7 * layers} FP8 linears of Qwen2.5-7B shape ({layers} layers), {tokens} tokens "
+                       f"over {world} GPUs (token rows; gate/up output columns)",
+           "n_gpus": world, "tokens": tokens, "layers": layers,
+           "nvlink_bytes_received_per_gpu_per_step": gather_bytes}
+    clock = ClockSampler(local)
+    clock.start()
+    if "codebook" in phases:
+        mismatch.zero_()
+        t = timed("codebook", args.c4_steps, args.c4_warmup)
+        ops = sum(2.0 * tokens * s.n * s.k for s in shapes_full) * layers
+        res["codebook"] = {"exact_tops": ops / (t * 1e-3) / 1e12, "ms_per_step": t,
+                           "exact_int_ops_per_step": ops}
+        torch.cuda.synchronize()
+        bad = mismatch.clone()
+        if world > 1:
+            dist.all_reduce(bad)
+        res["freivalds_mismatch_rows"] = int(bad.item())
+    if "hawkeye" in phases:
+        t = timed("hawkeye", max(1, args.c4_steps // 2), min(args.c4_warmup, 2))
+        outputs = sum(tokens * s.n for s in shapes_full) * layers
+        products = sum(tokens * s.n * s.k for s in shapes_full) * layers
+        res["hawkeye"] = {"outputs_per_s": outputs / (t * 1e-3), "products_per_s": products / (t * 1e-3),
+                          "ms_per_step": t}
+    res["clocks"] = clock.stop()
+    if rank == 0:
+        print(json.dumps({"c4": res}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -562,10 +732,18 @@ def main() -> None:
     ap.add_argument("--hawkeye-only", action="store_true", help="only the config-2 Hawkeye measurement")
     ap.add_argument("--hawkeye-tokens", type=int, default=16384)
     ap.add_argument("--hawkeye-steps", type=int, default=3)
+    ap.add_argument("--config4", action="store_true", help="the config-4 (7B shapes) multi-GPU measurement")
+    ap.add_argument("--c4-tokens", type=int, default=16384)
+    ap.add_argument("--c4-layers", type=int, default=28)
+    ap.add_argument("--c4-steps", type=int, default=4)
+    ap.add_argument("--c4-warmup", type=int, default=3)
+    ap.add_argument("--c4-phases", default="codebook,hawkeye")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.hawkeye_only:
+    if args.config4:
+        run_c4(args)
+    elif args.hawkeye_only:
         run_hawkeye(args)
     elif args.profile_step:
         run_profile_step(args)
