@@ -177,48 +177,30 @@ def measured_int32_issue_rate(device) -> float:
 
 def run_hawkeye(args, emit: bool = True) -> dict:
     """Config 2: direct Hawkeye replay of all 168 linears of the 0.5B shapes at
-    `--hawkeye-tokens` tokens (0.1 % x50 outliers).  One step = quantise, stage and replay
-    every linear (captured once in a CUDA graph).  Metric: Hawkeye outputs per second."""
+    `--hawkeye-tokens` tokens (0.1 % x50 outliers).  One step = quantise and stage every
+    linear, then replay every linear, the replays spread over four side streams (captured
+    once in a CUDA graph).  Metric: Hawkeye outputs per second."""
     from int_model_approximation_b200 import _native as nat
-    from int_model_approximation_b200.hawkeye import HawkeyeOperand
+    from int_model_approximation_b200.pipeline import HawkeyeStack
 
     world, rank, local = _dist()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    lib = nat.lib()
+    nat.lib()
     tokens = args.hawkeye_tokens
     shapes, weights, xs = build_workload(2, tokens, device, rank)
-    w_ops = [HawkeyeOperand(w) for w, _ws, _b in weights]
-    w_scales = [ws.reshape(-1).to(torch.float32).contiguous() for _w, ws, _b in weights]
-    kmax = max(s.k for s in shapes)
-    q = torch.empty((tokens, kmax), dtype=torch.uint8, device=device)
-    scale = torch.empty((tokens,), dtype=torch.float32, device=device)
-    xop = torch.empty((int(lib.ima_hawkeye_operand_bytes(tokens, kmax)),), dtype=torch.uint8, device=device)
-    ys = [torch.empty((tokens, s.n), dtype=torch.bfloat16, device=device) for s in shapes]
+    stack = HawkeyeStack(weights)
+    bufs = stack.allocate(tokens)
     stream = torch.cuda.Stream(device)
-
-    def forward(replay_only: bool = False):
-        sp = stream.cuda_stream
-        for i, s in enumerate(shapes):
-            if not replay_only:
-                x = xs[i]
-                nat.check("q", lib.ima_quantize_per_token(x.data_ptr(), nat.IMA_DTYPE_BF16, tokens, s.k, s.k,
-                                                          q.data_ptr(), s.k, scale.data_ptr(), None, s.k, None,
-                                                          None, 16, sp))
-                nat.check("p", lib.ima_hawkeye_prepare(q.data_ptr(), tokens, s.k, s.k, xop.data_ptr(), sp))
-            nat.check("r", lib.ima_hawkeye_replay(xop.data_ptr(), w_ops[i].buffer.data_ptr(), scale.data_ptr(),
-                                                  w_scales[i].data_ptr(), tokens, s.n, s.k, 32, 14, -139,
-                                                  ys[i].data_ptr(), s.n, None, s.n, sp))
-
     with torch.cuda.stream(stream):
-        forward()
+        stack.forward(xs, bufs)
     torch.cuda.synchronize()
     graphs = {}
     for name, ro in (("step", False), ("replay", True)):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             with torch.cuda.graph(g, stream=stream):
-                forward(replay_only=ro)
+                stack.forward(xs, bufs, replay_only=ro)
         graphs[name] = g
     steps = max(2, args.hawkeye_steps)
     times = {}
@@ -253,7 +235,7 @@ def run_hawkeye(args, emit: bool = True) -> dict:
             "peak_source": "ima_int32_issue_probe (XOR+ADD chains, all SMs) measured in this run",
             "products_per_s_replay_only": replay_terms,
         },
-        "launches_per_step": 3 * len(shapes),
+        "launches_per_step": stack.launches_per_forward(),
     }
     if emit and rank == 0:
         print(json.dumps({"hawkeye": res}), flush=True)
@@ -358,7 +340,7 @@ def run_b200(args) -> None:
         g1.record(stream)
     g1.synchronize()
     gemm_ms_per_step = g0.elapsed_time(g1) / args.steps
-    gemm_launches = stack.launches_per_forward() - 2
+    gemm_launches = len(stack._batches())
 
     # ---- end to end through the public API: host buffers in, host results out ----
     host_x = [x.cpu().pin_memory() for x in xs]
@@ -424,7 +406,7 @@ def run_b200(args) -> None:
                 "exact_int_ops_per_step_per_gpu": flops,
                 "l2": "inputs larger than L2 (about 2.4 GB of weight planes and activations per step)",
                 "launch": "one CUDA graph per step: grouped quantiser, grouped GEMM (up to 80 linears per "
-                          "launch), grouped Freivalds row check",
+                          "launch), grouped Freivalds row check of each GEMM launch on a side stream",
                 "parallelism": f"replicas x{world} (token batches per rank)",
             },
             "freivalds_mismatch_rows": mismatches,
@@ -638,18 +620,27 @@ def run_c4(args) -> None:
         else:
             drained[s].record(cs)
 
+    hk_side = [torch.cuda.Stream(device) for _ in range(4)]
+
     def hawkeye_layer(layer: int, s: int) -> None:
         sp_ = cs.cuda_stream
         b = sets[s]
         for p, sp in enumerate(specs):
-            rows, k, n = sp["rows"], sp["k"], sp["n"]
+            rows, k = sp["rows"], sp["k"]
             nat.check("q", lib.ima_quantize_per_token(xs[p].data_ptr(), nat.IMA_DTYPE_BF16, rows, k, k,
                                                       b["q"][p].data_ptr(), k, b["scale"][p].data_ptr(), None, k,
                                                       None, None, 16, sp_))
             nat.check("p", lib.ima_hawkeye_prepare(b["q"][p].data_ptr(), rows, k, k, hk_xop[p].data_ptr(), sp_))
+        for st in hk_side:   # replays round-robin on side streams (overlapping grid tails)
+            st.wait_stream(cs)
+        for p, sp in enumerate(specs):
+            rows, k, n = sp["rows"], sp["k"], sp["n"]
             nat.check("r", lib.ima_hawkeye_replay(hk_xop[p].data_ptr(), hk_w[layer][p].buffer.data_ptr(),
                                                   b["scale"][p].data_ptr(), hk_ws[layer][p].data_ptr(), rows, n, k,
-                                                  32, 14, -139, b["y"][p].data_ptr(), n, None, n, sp_))
+                                                  32, 14, -139, b["y"][p].data_ptr(), n, None, n,
+                                                  hk_side[p % len(hk_side)].cuda_stream))
+        for st in hk_side:
+            cs.wait_stream(st)
 
     def step(phase: str) -> None:
         for layer in range(layers):

@@ -156,6 +156,35 @@ def test_hawkeye_random_shapes_against_oracle(cuda_device, m, k, n):
     assert torch.equal(out.cpu().view(torch.int16), ref.view(torch.int16))
 
 
+def test_hawkeye_stack_matches_single_launches(cuda_device):
+    """HawkeyeStack (quantise + stage per linear, replays spread over side streams) gives
+    the same bits as hawkeye_fp8_sum on every linear."""
+    from int_model_approximation_b200.pipeline import HawkeyeStack
+
+    weights, xs = [], []
+    for i in range(9):
+        m, n, k = 40 + 17 * i, 30 + 45 * i, 64 + 90 * i
+        w, ws = synthetic.normal_fp8_weights(n, k, seed=2900 + i)
+        weights.append((w.to(cuda_device), ws.to(cuda_device), None))
+        xs.append(synthetic.student_t_activations(m, k, seed=3900 + i, outlier_fraction=0.02).to(cuda_device))
+    stack = HawkeyeStack(weights)
+    bufs = {"q": [], "scale": [], "xop": [], "y": []}
+    lib = nat.lib()
+    for (w, _ws, _b), x in zip(weights, xs):
+        m, k = x.shape
+        bufs["q"].append(torch.empty((m, k), dtype=torch.uint8, device=cuda_device))
+        bufs["scale"].append(torch.empty((m,), dtype=torch.float32, device=cuda_device))
+        bufs["xop"].append(torch.empty((int(lib.ima_hawkeye_operand_bytes(m, k)),), dtype=torch.uint8,
+                                       device=cuda_device))
+        bufs["y"].append(torch.empty((m, w.shape[0]), dtype=torch.bfloat16, device=cuda_device))
+    stack.forward(xs, bufs)
+    torch.cuda.synchronize()
+    for i, ((w, ws, _b), x) in enumerate(zip(weights, xs)):
+        xq, xsc, *_ = codebook.per_token_fp8(x)
+        ref, _ = hawkeye.hawkeye_fp8_sum(xq, xsc, w, ws)
+        assert torch.equal(bufs["y"][i].view(torch.int16), ref.view(torch.int16)), f"linear {i}"
+
+
 def test_hawkeye_raw_byte_patterns_against_oracle(cuda_device):
     g = torch.Generator().manual_seed(9)
     x = torch.randint(0, 256, (70, 160), generator=g, dtype=torch.int64).to(torch.uint8).view(torch.float8_e4m3fn)
@@ -479,9 +508,10 @@ def test_grouped_pipeline_matches_oracle_and_flags_corruption(cuda_device):
     bufs["c"][1][7, 3] += 1
     bufs["c"][3][149, 895] -= 5
     lib = nat.lib()
-    _q, _g, rows = bufs["_desc"]
+    _q, per_batch = bufs["_desc"]
     import ctypes
-    nat.check("rows", lib.ima_freivalds_rows_grouped(ctypes.byref(rows), len(shapes), nat.stream_of(cuda_device)))
+    for _g, rows, count in per_batch:
+        nat.check("rows", lib.ima_freivalds_rows_grouped(ctypes.byref(rows), count, nat.stream_of(cuda_device)))
     torch.cuda.synchronize()
     expected = int(stack.linears[1].r[3].item() != 0) + int(stack.linears[3].r[895].item() != 0)
     assert int(bufs["mismatch"].item()) == expected == 2
