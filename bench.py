@@ -605,17 +605,59 @@ def run_c4(args) -> None:
     gathered = [torch.empty((world * sp["rows"], sp["n"]), dtype=torch.bfloat16, device=device) for sp in specs]
     hk_xop = [torch.empty((int(lib.ima_hawkeye_operand_bytes(sp["rows"], sp["k"])),), dtype=torch.uint8,
                           device=device) for sp in specs] if "hawkeye" in phases else []
-    cs, ms = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    # the gathers get a high-priority stream, and the persistent GEMM leaves SMs to them
+    cs, ms = torch.cuda.Stream(device), torch.cuda.Stream(device, priority=-1)
+    reserve = args.c4_sm_reserve if args.c4_sm_reserve >= 0 else (16 if world > 1 and args.c4_gather == "nccl" else 0)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    nat.call("ima_set_gemm_sm_limit", max(sms - reserve, 1) if reserve else 0)
     computed = [torch.cuda.Event(), torch.cuda.Event()]
     drained = [torch.cuda.Event(), torch.cuda.Event()]
+
+    # Gather of the output shards.  "ce": every rank copies its shard into every rank's
+    # gathered buffer (shared once through CUDA IPC) with peer-to-peer copies on the copy
+    # engines, which use no SM and so overlap the compute fully; "nccl": one
+    # all_gather_into_tensor per linear.
+    use_ce = world > 1 and args.c4_gather == "ce"
+    peer_bufs, own_bufs = [], []
+    if use_ce:
+        import ctypes
+
+        hb = int(lib.ima_ipc_handle_bytes())
+        handles = []
+        for sp in specs:
+            ptr, h = ctypes.c_void_p(), (ctypes.c_char * hb)()
+            nat.call("ima_ipc_alloc", world * sp["rows"] * sp["n"] * 2, ctypes.byref(ptr), h)
+            own_bufs.append(ptr.value)
+            handles.append(bytes(h))
+        del gathered[:]
+        everyone = [None] * world
+        dist.all_gather_object(everyone, handles)
+        for q in range(world):
+            row = []
+            for p in range(len(specs)):
+                if q == rank:
+                    row.append(own_bufs[p])
+                else:
+                    ptr = ctypes.c_void_p()
+                    h = (ctypes.c_char * hb).from_buffer_copy(everyone[q][p])
+                    nat.call("ima_ipc_open", h, ctypes.byref(ptr))
+                    row.append(ptr.value)
+            peer_bufs.append(row)
 
     def gather(s: int) -> None:
         computed[s].record(cs)
         if world > 1:
             ms.wait_event(computed[s])
-            with torch.cuda.stream(ms):
-                for p in range(len(specs)):
-                    dist.all_gather_into_tensor(gathered[p], sets[s]["y"][p])
+            if use_ce:
+                for p, sp in enumerate(specs):
+                    shard = sp["rows"] * sp["n"] * 2
+                    src = sets[s]["y"][p].data_ptr()
+                    for q in range(world):
+                        nat.call("ima_copy_async", peer_bufs[q][p] + rank * shard, src, shard, ms.cuda_stream)
+            else:
+                with torch.cuda.stream(ms):
+                    for p in range(len(specs)):
+                        dist.all_gather_into_tensor(gathered[p], sets[s]["y"][p])
             drained[s].record(ms)
         else:
             drained[s].record(cs)
@@ -680,8 +722,10 @@ def run_c4(args) -> None:
     gather_bytes = sum(2 * (world - 1) * sp["rows"] * sp["n"] for sp in specs) * layers if world > 1 else 0
     res = {"workload": f"c4: {7 * layers} FP8 linears of Qwen2.5-7B shape ({layers} layers), {tokens} tokens "
                        f"over {world} GPUs (token rows; gate/up output columns)",
-           "n_gpus": world, "tokens": tokens, "layers": layers,
-           "nvlink_bytes_received_per_gpu_per_step": gather_bytes}
+           "n_gpus": world, "tokens": tokens, "layers": layers, "gemm_sms_left_to_collectives": reserve,
+           "nvlink_bytes_received_per_gpu_per_step": gather_bytes,
+           "gather": ("copy engines: peer-to-peer copies into CUDA-IPC-shared buffers" if use_ce else
+                      "NCCL all_gather_into_tensor") if world > 1 else None}
     clock = ClockSampler(local)
     clock.start()
     if "codebook" in phases:
@@ -705,7 +749,15 @@ def run_c4(args) -> None:
     if rank == 0:
         print(json.dumps({"c4": res}), flush=True)
     if world > 1:
-        dist.barrier()
+        torch.cuda.synchronize()
+        dist.barrier()   # every rank's copies into the shared buffers are done
+        for q in range(len(peer_bufs)):
+            if q != rank:
+                for ptr in peer_bufs[q]:
+                    nat.call("ima_ipc_close", ptr)
+        dist.barrier()   # every peer has unmapped this rank's buffers
+        for ptr in own_bufs:
+            nat.call("ima_ipc_free", ptr)
         dist.destroy_process_group()
 
 
@@ -729,6 +781,9 @@ def main() -> None:
     ap.add_argument("--c4-steps", type=int, default=4)
     ap.add_argument("--c4-warmup", type=int, default=3)
     ap.add_argument("--c4-phases", default="codebook,hawkeye")
+    ap.add_argument("--c4-sm-reserve", type=int, default=-1,
+                    help="SMs the GEMM leaves to the gather kernels (-1: 16 with NCCL gathers, 0 otherwise)")
+    ap.add_argument("--c4-gather", choices=["ce", "nccl"], default="ce")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

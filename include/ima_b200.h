@@ -64,6 +64,19 @@ int ima_quant_fast_selftest(int kind, unsigned long long* mismatches, void* stre
  * word of `device`.  code == IMA_OK when no kernel recorded a failure. */
 int ima_device_status(int device, int* code, int* where, int* detail, int clear);
 
+/* ---- multi-GPU plumbing (no reference counterpart) -----------------------------
+ * Collectives on the copy engines: a process allocates a device buffer it shares with
+ * the other processes of the node (ima_ipc_alloc returns the pointer and an opaque handle
+ * of ima_ipc_handle_bytes() bytes to send to them), a peer maps it with ima_ipc_open, and
+ * ima_copy_async copies into it (peer to peer over NVLink, no kernel: it uses no SM).
+ * ima_ipc_close unmaps a peer's buffer, ima_ipc_free releases one's own. */
+int ima_ipc_handle_bytes(void);
+int ima_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+int ima_ipc_free(void* ptr);
+int ima_ipc_open(const void* handle, void** ptr);
+int ima_ipc_close(void* ptr);
+int ima_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+
 /* ---- A1/A2: per-token FP8 quantiser -----------------------------------------
  * ref: __main__.py:148-154 _per_token_fp8, :157-158 _fp8_e4m3_to_int32,
  *      :161-163 _per_token_fp8_int32.
@@ -159,6 +172,11 @@ typedef struct ima_gemm_problem {
     int64_t ldy;
 } ima_gemm_problem;
 int ima_int_gemm_grouped(const ima_gemm_problem* problems, int count, int scheme, void* stream);
+/* Process-wide cap on the number of persistent GEMM CTAs (one per SM); 0 (the default)
+ * uses every SM.  A multi-GPU caller leaves a few SMs to the collectives it overlaps with
+ * the GEMM (a persistent CTA never yields its SM, so a collective kernel queued behind a
+ * full-machine GEMM launch would otherwise wait for it).  No reference counterpart. */
+int ima_set_gemm_sm_limit(int sms);
 
 /* ---- A4: direct Hawkeye replay ---------------------------------------------
  * ref: hawkeye.py:222-275 hawkeye_fp8_sum (kernel hawkeye.py:127-219).

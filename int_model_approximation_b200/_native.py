@@ -76,6 +76,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ima_quant_fast_selftest": (_I32, [_I32, _VP, _VP]),
     "ima_quantize_grouped": (_I32, [_VP, _I32, _VP]),
     "ima_int_gemm_grouped": (_I32, [_VP, _I32, _I32, _VP]),
+    "ima_set_gemm_sm_limit": (_I32, [_I32]),
+    "ima_ipc_handle_bytes": (_I32, []),
+    "ima_ipc_alloc": (_I32, [_I64, _VP, _VP]),
+    "ima_ipc_free": (_I32, [_VP]),
+    "ima_ipc_open": (_I32, [_VP, _VP]),
+    "ima_ipc_close": (_I32, [_VP]),
+    "ima_copy_async": (_I32, [_VP, _VP, _I64, _VP]),
     "ima_freivalds_weight_vector": (_I32, [_VP, _I64, _VP, _I64, _I64, _VP, _VP]),
     "ima_freivalds_rows_grouped": (_I32, [_VP, _I32, _VP]),
     "ima_status_string": (ctypes.c_char_p, [_I32]),

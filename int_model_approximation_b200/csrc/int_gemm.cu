@@ -471,6 +471,14 @@ int num_sms() {
     return n;
 }
 
+// Upper bound on the persistent GEMM grid (0: every SM); see ima_set_gemm_sm_limit.
+int g_gemm_sm_limit = 0;
+
+int gemm_grid_limit() {
+    const int n = num_sms();
+    return (g_gemm_sm_limit > 0 && g_gemm_sm_limit < n) ? g_gemm_sm_limit : n;
+}
+
 int check_problem(const ima_gemm_problem& q, int scheme) {
     if (!q.a_planes || !q.b_planes || q.M < 0 || q.N < 0 || q.K < 0) return IMA_ERR_INVALID_ARGUMENT;
     if (!q.c && !q.y) return IMA_ERR_INVALID_ARGUMENT;
@@ -495,7 +503,8 @@ int launch_batch(GemmBatch& b, cudaStream_t stream) {
     if (rc != IMA_OK) return rc;
     int64_t tiles = b.tile_start[b.n];
     if (tiles == 0) return IMA_OK;
-    int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+    const int limit = gemm_grid_limit();
+    int grid = (int)(tiles < limit ? tiles : limit);
     kern<<<grid, GM_THREADS, L::ALLOC, stream>>>(b);
     return IMA_LAUNCH_STATUS();
 }
@@ -559,6 +568,12 @@ int run_grouped(const ima_gemm_problem* problems, int count, cudaStream_t stream
 }
 
 }  // namespace
+
+extern "C" int ima_set_gemm_sm_limit(int sms) {
+    if (sms < 0) return IMA_ERR_INVALID_ARGUMENT;
+    g_gemm_sm_limit = sms;
+    return IMA_OK;
+}
 
 extern "C" int ima_int_gemm_grouped(const ima_gemm_problem* problems, int count, int scheme, void* stream) {
     if (count < 0 || (count > 0 && !problems)) return IMA_ERR_INVALID_ARGUMENT;

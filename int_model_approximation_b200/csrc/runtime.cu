@@ -84,3 +84,44 @@ int ima_device_status(int device, int* code, int* where, int* detail, int clear)
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Multi-GPU plumbing for collectives on the copy engines: device buffers shared between
+// the processes of one node through CUDA IPC, and asynchronous copies into a peer's
+// buffer (peer-to-peer over NVLink, no kernel).  No reference counterpart.
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int ima_ipc_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int ima_ipc_alloc(int64_t bytes, void** ptr, void* handle) {
+    if (bytes <= 0 || !ptr || !handle) return IMA_ERR_INVALID_ARGUMENT;
+    *ptr = nullptr;
+    int rc = ima_note_cuda(cudaMalloc(ptr, (size_t)bytes));
+    if (rc != IMA_OK) return rc;
+    rc = ima_note_cuda(cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle), *ptr));
+    if (rc != IMA_OK) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+    }
+    return rc;
+}
+
+int ima_ipc_free(void* ptr) { return ptr ? ima_note_cuda(cudaFree(ptr)) : IMA_OK; }
+
+int ima_ipc_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return IMA_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return ima_note_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int ima_ipc_close(void* ptr) { return ptr ? ima_note_cuda(cudaIpcCloseMemHandle(ptr)) : IMA_OK; }
+
+int ima_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+    if (bytes < 0 || (bytes > 0 && (!dst || !src))) return IMA_ERR_INVALID_ARGUMENT;
+    if (bytes == 0) return IMA_OK;
+    return ima_note_cuda(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, (cudaStream_t)stream));
+}
+
+}  // extern "C"
