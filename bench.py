@@ -644,17 +644,27 @@ def run_c4(args) -> None:
                     row.append(ptr.value)
             peer_bufs.append(row)
 
+    # one copy stream per destination rank, so that several copy engines push at once
+    ce_streams = [torch.cuda.Stream(device, priority=-1) for _ in range(world)] if use_ce else []
+    ce_done = [[torch.cuda.Event() for _ in range(world)] for _ in range(2)] if use_ce else []
+
     def gather(s: int) -> None:
         computed[s].record(cs)
         if world > 1:
-            ms.wait_event(computed[s])
             if use_ce:
-                for p, sp in enumerate(specs):
-                    shard = sp["rows"] * sp["n"] * 2
-                    src = sets[s]["y"][p].data_ptr()
-                    for q in range(world):
-                        nat.call("ima_copy_async", peer_bufs[q][p] + rank * shard, src, shard, ms.cuda_stream)
+                for q in range(world):
+                    st = ce_streams[(rank + q) % world]   # start at different peers on different ranks
+                    dst_rank = (rank + q) % world
+                    st.wait_event(computed[s])
+                    for p, sp in enumerate(specs):
+                        shard = sp["rows"] * sp["n"] * 2
+                        nat.call("ima_copy_async", peer_bufs[dst_rank][p] + rank * shard, sets[s]["y"][p].data_ptr(),
+                                 shard, st.cuda_stream)
+                    ce_done[s][q].record(st)
+                for q in range(world):
+                    ms.wait_event(ce_done[s][q])
             else:
+                ms.wait_event(computed[s])
                 with torch.cuda.stream(ms):
                     for p in range(len(specs)):
                         dist.all_gather_into_tensor(gathered[p], sets[s]["y"][p])
@@ -788,6 +798,9 @@ def main() -> None:
     if args.warmup < 3:
         args.warmup = 3
     if args.config4:
+        # compute, gather, check and per-peer copy streams: more than the default 8 hardware
+        # queues, which would serialise unrelated streams (must be set before CUDA starts)
+        os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
         run_c4(args)
     elif args.hawkeye_only:
         run_hawkeye(args)
