@@ -372,6 +372,8 @@ def _small_class_count_case(device):
         dict(class_chunk=16, packed_count_lanes=6, packed_group_lanes=2),
         dict(class_chunk=32, cache_weight_chunks=True),
         dict(class_chunk=8, count_dtype=torch.int8),
+        dict(class_chunk=8, packed_count_lanes=6, packed_group_lanes=3),
+        dict(class_chunk=4, packed_count_lanes=6, packed_group_lanes=6),
     ],
 )
 def test_class_counts_with_an_injected_raw_matmul(cuda_device, params):

@@ -259,3 +259,21 @@ def test_cached_weight_chunk_product_equals_the_plain_product():
                                                                                   _cpu_matmul)
     plain, _, _ = hawkeye_freivalds._class_chunk_product_raw(a_cls, b_cls, a_classes, b_classes, _cpu_matmul)
     assert (a_size, b_size) == (6, 3) and torch.equal(flat, plain)
+
+
+def test_codebook_stack_batches_balance_cost_within_the_launch_limit():
+    """Problems are dealt to ceil(n / GEMM_BATCH) launches, each at most GEMM_BATCH problems,
+    every problem exactly once, launch costs within one largest problem of each other."""
+    from types import SimpleNamespace
+
+    from int_model_approximation_b200.pipeline import CodebookStack
+
+    stack = CodebookStack.__new__(CodebookStack)
+    shapes = [(896, 896), (128, 896), (128, 896), (896, 896), (4864, 896), (4864, 896), (896, 4864)] * 24
+    stack.linears = [SimpleNamespace(n=n, k=k) for n, k in shapes]
+    batches = stack._batches()
+    assert len(batches) == -(-len(shapes) // CodebookStack.GEMM_BATCH)
+    assert sorted(i for b in batches for i in b) == list(range(len(shapes)))
+    assert all(len(b) <= CodebookStack.GEMM_BATCH for b in batches)
+    costs = [sum(shapes[i][0] * shapes[i][1] for i in b) for b in batches]
+    assert max(costs) - min(costs) <= max(n * k for n, k in shapes)
