@@ -7,8 +7,14 @@ epilogue) with full int64 outputs, and a Freivalds check of every product.
 A "step" is one forward of all 168 linears.  Metric: exact int GEMM TOPS =
 sum over linears of 2*M*N*K / step time (whole job, all GPUs).
 
+At N = 1 the line also carries "hawkeye_c2": the config-2 measurement (all 168 linears at
+16384 tokens through the direct Hawkeye replay; outputs/s, products/s, INT-issue roofline).
+
 N > 1 (torchrun): every rank runs the same workload on its own token batch (weak
 scaling); the only collective is an all-reduce of the Freivalds mismatch counter.
+
+--config4 runs the config-4 (Qwen2.5-7B shapes, 16384 tokens) multi-GPU measurement,
+--hawkeye-only the config-2 measurement alone.
 
 --impl reference times the reference's CPU path (its torch expressions: per-token
 quantiser, torch int64 matmul, fp32 rescale) on the host cores over a bounded sample.
@@ -438,6 +444,13 @@ def run_b200(args) -> None:
             "cpu_baseline": cpu,
             "measured_peaks": {k: peaks.get(k) for k in ("hbm_gbs", "bf16_tflops")},
         }
+        if world == 1 and not args.no_hawkeye:
+            # the other half of the metric: config-2 Hawkeye replay outputs/s (a failure here
+            # is reported in the line and does not cost the codebook measurement)
+            try:
+                line["hawkeye_c2"] = run_hawkeye(args, emit=False)
+            except Exception as exc:  # noqa: BLE001
+                line["hawkeye_c2"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         print(json.dumps(line), flush=True)
     if world > 1:
         del graph, gemm_graph
@@ -785,6 +798,7 @@ def main() -> None:
     ap.add_argument("--hawkeye-only", action="store_true", help="only the config-2 Hawkeye measurement")
     ap.add_argument("--hawkeye-tokens", type=int, default=16384)
     ap.add_argument("--hawkeye-steps", type=int, default=3)
+    ap.add_argument("--no-hawkeye", action="store_true", help="skip the config-2 Hawkeye object of the default line")
     ap.add_argument("--config4", action="store_true", help="the config-4 (7B shapes) multi-GPU measurement")
     ap.add_argument("--c4-tokens", type=int, default=16384)
     ap.add_argument("--c4-layers", type=int, default=28)
