@@ -1,6 +1,6 @@
 """Benchmark of the B200 student-linear hot path (prints ONE JSON line on rank 0).
 
-Workload (N = 1 GPU): BASELINE config 1 -- all 168 FP8 linears of a random-init
+Workload (N = 1 GPU): configuration 1 -- all 168 FP8 linears of a random-init
 Qwen2.5-0.5B-shaped model, 512 tokens each, codebook student: per-token e4m3
 quantisation, the exact int64 GEMM (tcgen05 kind::i8, fused rescale/bias/bf16
 epilogue) with full int64 outputs, and a Freivalds check of every product.

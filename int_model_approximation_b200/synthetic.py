@@ -101,7 +101,9 @@ def qwen7b_linears() -> list[LinearShape]:
     return out
 
 
-# The five BASELINE configurations.
+# The five benchmark configurations (0: one gate_proj linear at 16 tokens; 1-2: the 0.5B
+# shapes, codebook at 512 tokens and Hawkeye at 16384; 3: down_proj class counts; 4: the 7B
+# shapes at 16384 tokens).
 CONFIGS = {
     0: dict(name="c0-gate-16tok", linears=[LinearShape("gate_proj", 4864, 896)], tokens=16, outliers=0.0),
     1: dict(name="c1-qwen0.5b-codebook-512tok", linears=None, tokens=512, outliers=0.0),
