@@ -184,8 +184,8 @@ def measured_int32_issue_rate(device) -> float:
 def run_hawkeye(args, emit: bool = True) -> dict:
     """Config 2: direct Hawkeye replay of all 168 linears of the 0.5B shapes at
     `--hawkeye-tokens` tokens (0.1 % x50 outliers).  One step = quantise and stage every
-    linear, then replay every linear, the replays spread over four side streams (captured
-    once in a CUDA graph).  Metric: Hawkeye outputs per second."""
+    linear, then replay every linear, the replays spread over four side streams (each phase
+    captured once in a CUDA graph).  Metric: Hawkeye outputs per second."""
     from int_model_approximation_b200 import _native as nat
     from int_model_approximation_b200.pipeline import HawkeyeStack
 
@@ -201,26 +201,30 @@ def run_hawkeye(args, emit: bool = True) -> dict:
     with torch.cuda.stream(stream):
         stack.forward(xs, bufs)
     torch.cuda.synchronize()
-    graphs = {}
-    for name, ro in (("step", False), ("replay", True)):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
+    # the two phases as CUDA graphs replayed back to back; events between them time the
+    # replay inside the timed steps
+    graphs = {name: torch.cuda.CUDAGraph() for name in ("prepare", "replay")}
+    with torch.cuda.stream(stream):
+        for name, g in graphs.items():
             with torch.cuda.graph(g, stream=stream):
-                stack.forward(xs, bufs, replay_only=ro)
-        graphs[name] = g
+                getattr(stack, name)(xs, bufs)
     steps = max(2, args.hawkeye_steps)
-    times = {}
-    for name, g in graphs.items():
-        with torch.cuda.stream(stream):
-            for _ in range(2):
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            for g in graphs.values():
                 g.replay()
-            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s_ev.record(stream)
-            for _ in range(steps):
-                g.replay()
-            e_ev.record(stream)
-        e_ev.synchronize()
-        times[name] = s_ev.elapsed_time(e_ev) / steps
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(2 * steps + 1)]
+        marks[0].record(stream)
+        for i in range(steps):
+            graphs["prepare"].replay()
+            marks[2 * i + 1].record(stream)
+            graphs["replay"].replay()
+            marks[2 * i + 2].record(stream)
+    marks[-1].synchronize()
+    times = {
+        "step": marks[0].elapsed_time(marks[-1]) / steps,
+        "replay": sum(marks[2 * i + 1].elapsed_time(marks[2 * i + 2]) for i in range(steps)) / steps,
+    }
     outputs = sum(tokens * s.n for s in shapes)
     products = sum(tokens * s.n * s.k for s in shapes)
     int_peak = measured_int32_issue_rate(device)
@@ -239,7 +243,7 @@ def run_hawkeye(args, emit: bool = True) -> dict:
             "unit": "G int ops/s (10 int ops per product, the reference's per-product op count)",
             "frac": round(10.0 * replay_terms / 1e9 / int_peak, 4),
             "peak_source": "ima_int32_issue_probe (XOR+ADD chains, all SMs) measured in this run",
-            "products_per_s_replay_only": replay_terms,
+            "products_per_s_replay_phase": replay_terms,
         },
         "launches_per_step": stack.launches_per_forward(),
     }
@@ -311,21 +315,27 @@ def run_b200(args) -> None:
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
+    # The step's three phases, each captured once into its own CUDA graph and replayed back
+    # to back on one stream, so that CUDA events between them time each kernel inside the
+    # timed region (the whole forward, one graph, serves the end-to-end loop below).
     graph = torch.cuda.CUDAGraph()
+    phase_graphs = {name: torch.cuda.CUDAGraph() for name in ("quantize", "multiply", "verify")}
     with torch.cuda.stream(stream):
         stack.forward(xs, bufs)
         torch.cuda.synchronize()
         with torch.cuda.graph(graph, stream=stream):
             stack.forward(xs, bufs)
-    # GEMM-only graph (for the roofline of the dominant kernel)
-    gemm_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        with torch.cuda.graph(gemm_graph, stream=stream):
-            stack.forward(xs, bufs, gemm_only=True)
+        for name, g in phase_graphs.items():
+            with torch.cuda.graph(g, stream=stream):
+                getattr(stack, name)(xs, bufs)
     torch.cuda.synchronize()
+    phase_ms = {name: 0.0 for name in phase_graphs}
 
-    def step():
-        graph.replay()
+    def step(marks: list | None = None):
+        for k, g in enumerate(phase_graphs.values()):
+            g.replay()
+            if marks is not None:
+                marks[k].record(stream)
         if world > 1:
             torch.distributed.all_reduce(bufs["mismatch"])
 
@@ -336,6 +346,7 @@ def run_b200(args) -> None:
     bufs["mismatch"].zero_()
 
     # ---- timed region (device resident inputs; inputs 2.4 GB per step > L2) ----
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in phase_graphs] for _ in range(args.steps)]
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -345,31 +356,32 @@ def run_b200(args) -> None:
     s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         s_ev.record(stream)
-        for _ in range(args.steps):
-            step()
+        for i in range(args.steps):
+            step(marks[i])
         e_ev.record(stream)
     e_ev.synchronize()
     clocks = sampler.stop()
     ms = s_ev.elapsed_time(e_ev) / args.steps
+    # per-phase device time: from the end of the previous mark (the step's start for the
+    # quantiser, which includes the previous step's mismatch all-reduce when world > 1)
+    for i in range(args.steps):
+        prev = s_ev if i == 0 else marks[i - 1][-1]
+        for k, name in enumerate(phase_graphs):
+            phase_ms[name] += prev.elapsed_time(marks[i][k]) / args.steps
+            prev = marks[i][k]
     if world > 1:
-        t = torch.tensor([ms], device=device)
+        t = torch.tensor([ms] + list(phase_ms.values()), device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = float(t[0].item())
+        phase_ms = dict(zip(phase_ms, (float(v) for v in t[1:].tolist())))
         torch.distributed.barrier()
     mismatches = int(bufs["mismatch"].item())
-
-    # ---- dominant kernel: the GEMMs alone, same stream, CUDA events ----
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            gemm_graph.replay()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for _ in range(args.steps):
-            gemm_graph.replay()
-        g1.record(stream)
-    g1.synchronize()
-    gemm_ms_per_step = g0.elapsed_time(g1) / args.steps
+    gemm_ms_per_step = phase_ms["multiply"]
     gemm_launches = len(stack._batches())
+    # algorithmic bytes of the Freivalds row pass: fp8 codes of A, int64 C, int64 r and t
+    check_bytes = sum(TOKENS * s.k + 8 * TOKENS * s.n + 8 * s.n + 8 * s.k for s in shapes)
+    # quantiser: bf16 activations in; e4m3 codes and three digit-plane bytes out per element
+    quant_bytes = sum(TOKENS * s.k * (2 + 1 + 3) + 8 * TOKENS for s in shapes)
 
     # ---- end to end through the public API: host buffers in, host results out ----
     # Every step copies its activations in from pinned host memory and its bf16 outputs and
@@ -470,8 +482,8 @@ def run_b200(args) -> None:
                 "tokens_per_gpu": TOKENS,
                 "exact_int_ops_per_step_per_gpu": flops,
                 "l2": "inputs larger than L2 (about 2.4 GB of weight planes and activations per step)",
-                "launch": "one CUDA graph per step: grouped quantiser, grouped GEMM (up to 80 linears per "
-                          "launch), grouped Freivalds row check of each GEMM launch on a side stream",
+                "launch": "three CUDA graphs per step on one stream: grouped quantiser, grouped GEMM (up to "
+                          "80 linears per launch), Freivalds row check of every product (one launch)",
                 "parallelism": f"replicas x{world} (token batches per rank)",
             },
             "freivalds_mismatch_rows": mismatches,
@@ -489,6 +501,30 @@ def run_b200(args) -> None:
                 "gemm_ms_per_step": round(gemm_ms_per_step, 4),
                 "gemm_launches_per_step": gemm_launches,
                 "exact_tops_gemm_only": round(flops / (gemm_ms_per_step * 1e-3) / 1e12, 3),
+                "timing": "CUDA events around the GEMM launches inside the timed steps",
+            },
+            "phases_ms_per_step": {k: round(v, 4) for k, v in phase_ms.items()},
+            "freivalds_roofline": {
+                "kernel": "fv_rows_aligned_kernel",
+                "bound": "hbm",
+                "achieved": round(check_bytes / (phase_ms["verify"] * 1e-3) / 1e9, 1),
+                "peak": peaks.get("hbm_gbs"),
+                "unit": "GB/s",
+                "frac": round(check_bytes / (phase_ms["verify"] * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)
+                if peaks.get("hbm_gbs") else None,
+                "bytes_per_step": check_bytes,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy bandwidth)",
+            },
+            "quantizer_roofline": {
+                "kernel": "quantize_rows_kernel",
+                "bound": "hbm",
+                "achieved": round(quant_bytes / (phase_ms["quantize"] * 1e-3) / 1e9, 1),
+                "peak": peaks.get("hbm_gbs"),
+                "unit": "GB/s",
+                "frac": round(quant_bytes / (phase_ms["quantize"] * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)
+                if peaks.get("hbm_gbs") else None,
+                "bytes_per_step": quant_bytes,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy bandwidth)",
             },
             "e2e": {
                 "value": round(total_ops / (e2e_ms * 1e-3) / 1e12, 3),
@@ -514,7 +550,7 @@ def run_b200(args) -> None:
                 line["hawkeye_c2"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         print(json.dumps(line), flush=True)
     if world > 1:
-        del graph, gemm_graph
+        del graph, phase_graphs
         torch.distributed.destroy_process_group()
 
 

@@ -6,12 +6,11 @@ weight half of the check t = codebook(W)^T r, both fixed) and runs one forward o
 of them -- per-token quantisation, the exact int64 GEMM with the fused
 rescale/bias/bf16 epilogue, and the Freivalds row check of every int64 product -- as
 grouped launches (one quantiser launch, one GEMM launch per 80 linears, one Freivalds
-launch per GEMM launch on a side stream), entirely on the device and without host
-synchronisation.  The launch sequence can be captured once into a CUDA graph and
-replayed.
+launch for all products), entirely on the device and without host synchronisation.  The
+three phases can be run (and captured into CUDA graphs) separately or together.
 
-`HawkeyeStack` does the same for the direct Hawkeye replay student (replays spread over
-side streams).
+`HawkeyeStack` does the same for the direct Hawkeye replay student (quantise and stage,
+then replays spread over side streams).
 """
 
 from __future__ import annotations
@@ -40,7 +39,8 @@ class PreparedLinear:
 
 
 class CodebookStack:
-    GEMM_BATCH = 80   # problems per GEMM launch (kernel-parameter budget of the C side)
+    GEMM_BATCH = 80    # problems per GEMM launch (kernel-parameter budget of the C side)
+    CHECK_BATCH = 192  # products per Freivalds row-pass launch (kernel-parameter budget of the C side)
 
     def __init__(self, weights: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]], *, seed: int = 0):
         self.linears: list[PreparedLinear] = []
@@ -103,12 +103,19 @@ class CodebookStack:
             f.c, f.ldc, f.r = bufs["c"][i].data_ptr(), lin.n, lin.r.data_ptr()
             f.M, f.N, f.K, f.a_kind = m, lin.n, lin.k, nat.IMA_FREIVALDS_A_FP8
             f.mismatch_rows = bufs["mismatch"].data_ptr()
-        per_batch = []
+        gemm_batches = []
         for members in self._batches():
             g_arr = (nat.GemmProblem * len(members))(*[gemm[i] for i in members])
-            f_arr = (nat.FreivaldsRowsProblem * len(members))(*[rows[i] for i in members])
-            per_batch.append((g_arr, f_arr, len(members)))
-        return quant, per_batch
+            gemm_batches.append((g_arr, len(members)))
+        return quant, gemm_batches, rows
+
+    def _prepared(self, xs: list[torch.Tensor], bufs: dict) -> tuple:
+        """Launch descriptors for these activations and buffers (built once, then reused)."""
+        key = tuple(x.data_ptr() for x in xs)
+        if bufs.get("_key") != key:
+            bufs["_desc"] = self._descriptors(xs, bufs)
+            bufs["_key"] = key
+        return bufs["_desc"]
 
     def _batches(self) -> list[list[int]]:
         """Problems dealt to ceil(n / GEMM_BATCH) GEMM launches, largest first onto the least
@@ -123,44 +130,49 @@ class CodebookStack:
             loads[b] += self.linears[i].n * self.linears[i].k
         return [sorted(m) for m in members if m]
 
-    def forward(self, xs: list[torch.Tensor], bufs: dict, *, check: bool = True, gemm_only: bool = False) -> None:
+    def quantize(self, xs: list[torch.Tensor], bufs: dict) -> None:
+        """Per-token quantisation of every activation xs[i] [tokens, K_i] (bf16) into its
+        e4m3 codes, scales and digit planes: one launch."""
+        quant, _g, _f = self._prepared(xs, bufs)
+        main = torch.cuda.current_stream(self.device)
+        nat.check("ima_quantize_grouped",
+                  nat.lib().ima_quantize_grouped(ctypes.byref(quant), len(self.linears), main.cuda_stream))
+
+    def multiply(self, xs: list[torch.Tensor], bufs: dict) -> None:
+        """The exact int64 GEMM with the fused rescale/bias/bf16 epilogue of every linear
+        (reads the planes that quantize() wrote): a few cost-balanced grouped launches."""
+        _q, gemm_batches, _f = self._prepared(xs, bufs)
+        main = torch.cuda.current_stream(self.device)
+        for g_arr, count in gemm_batches:
+            nat.check("ima_int_gemm_grouped", nat.lib().ima_int_gemm_grouped(
+                ctypes.byref(g_arr), count, nat.IMA_SCHEME_DIGITS3, main.cuda_stream))
+
+    def verify(self, xs: list[torch.Tensor], bufs: dict) -> None:
+        """The Freivalds row check of every int64 product that multiply() wrote, failed rows
+        accumulated into bufs["mismatch"]: one row-pass launch over all products (the C side
+        splits it when there are more than CHECK_BATCH)."""
+        _q, _g, rows = self._prepared(xs, bufs)
+        main = torch.cuda.current_stream(self.device)
+        nat.check("ima_freivalds_rows_grouped",
+                  nat.lib().ima_freivalds_rows_grouped(ctypes.byref(rows), len(self.linears), main.cuda_stream))
+
+    def forward(self, xs: list[torch.Tensor], bufs: dict, *, check: bool = True) -> None:
         """One forward of every linear on activations xs[i] [tokens, K_i] (bf16).
 
         Writes bufs["c"][i] (exact int64 products), bufs["y"][i] (bf16 outputs) and
-        accumulates failed Freivalds rows into bufs["mismatch"].  Launches only.  The GEMM
-        runs as a few cost-balanced grouped launches; the Freivalds row check of launch i
-        runs on a side stream while launch i + 1 multiplies (a check CTA fits beside the
-        persistent GEMM CTA of every SM), and the current stream waits for it at the end."""
-        key = tuple(x.data_ptr() for x in xs)
-        if bufs.get("_key") != key:
-            bufs["_desc"] = self._descriptors(xs, bufs)
-            bufs["_key"] = key
-        quant, per_batch = bufs["_desc"]
-        n = len(self.linears)
-        lib = nat.lib()
-        main = torch.cuda.current_stream(self.device)
-        if not gemm_only:
-            nat.check("ima_quantize_grouped", lib.ima_quantize_grouped(ctypes.byref(quant), n, main.cuda_stream))
-        side = self._side_stream()
-        for g_arr, f_arr, count in per_batch:
-            nat.check("ima_int_gemm_grouped",
-                      lib.ima_int_gemm_grouped(ctypes.byref(g_arr), count, nat.IMA_SCHEME_DIGITS3, main.cuda_stream))
-            if check and not gemm_only:
-                side.wait_stream(main)
-                nat.check("ima_freivalds_rows_grouped",
-                          lib.ima_freivalds_rows_grouped(ctypes.byref(f_arr), count, side.cuda_stream))
-        if check and not gemm_only:
-            main.wait_stream(side)
-
-    def _side_stream(self) -> torch.cuda.Stream:
-        s = getattr(self, "_side", None)
-        if s is None:
-            s = self._side = torch.cuda.Stream(self.device)
-        return s
+        accumulates failed Freivalds rows into bufs["mismatch"].  Launches only, all on the
+        current stream: quantize(), multiply(), then verify().  The check runs after the
+        last GEMM launch with the whole GPU to itself; overlapping it with the GEMMs on a
+        side stream was measured slower, because its warps then get only the registers
+        that the persistent GEMM CTAs leave on each SM."""
+        self.quantize(xs, bufs)
+        self.multiply(xs, bufs)
+        if check:
+            self.verify(xs, bufs)
 
     def launches_per_forward(self, check: bool = True) -> int:
-        gemm = len(self._batches())
-        return 1 + gemm + (gemm if check else 0)
+        checks = -(-len(self.linears) // self.CHECK_BATCH)
+        return 1 + len(self._batches()) + (checks if check else 0)
 
 
 class HawkeyeStack:
@@ -184,24 +196,27 @@ class HawkeyeStack:
 
     REPLAY_STREAMS = 4
 
-    def forward(self, xs: list[torch.Tensor], bufs: dict, *, replay_only: bool = False) -> None:
-        """Quantise and stage every activation (two launches per linear), then replay the
-        linears round-robin on REPLAY_STREAMS side streams that fork from and join back to
-        the current stream: the last partial wave of one linear's grid overlaps the next
-        linear's first (measured 15 % faster than one stream at the c2 shapes).
-        replay_only skips the first part (for timing the replay alone).  Launches only."""
+    def prepare(self, xs: list[torch.Tensor], bufs: dict) -> None:
+        """Quantise and stage every activation xs[i] [tokens, K_i] (two launches per linear)."""
         lib = nat.lib()
         main = torch.cuda.current_stream(self.device)
-        if not replay_only:
-            for i, (w, _ws) in enumerate(self.weights):
-                x = xs[i]
-                m, k = int(x.shape[0]), int(x.shape[1])
-                q, scale, xop = bufs["q"][i], bufs["scale"][i], bufs["xop"][i]
-                nat.check("ima_quantize_per_token", lib.ima_quantize_per_token(
-                    x.data_ptr(), nat.dtype_code(x.dtype), m, k, x.stride(0), q.data_ptr(), k, scale.data_ptr(), None,
-                    k, None, None, 16, main.cuda_stream))
-                nat.check("ima_hawkeye_prepare", lib.ima_hawkeye_prepare(q.data_ptr(), m, k, k, xop.data_ptr(),
-                                                                         main.cuda_stream))
+        for i, (w, _ws) in enumerate(self.weights):
+            x = xs[i]
+            m, k = int(x.shape[0]), int(x.shape[1])
+            q, scale, xop = bufs["q"][i], bufs["scale"][i], bufs["xop"][i]
+            nat.check("ima_quantize_per_token", lib.ima_quantize_per_token(
+                x.data_ptr(), nat.dtype_code(x.dtype), m, k, x.stride(0), q.data_ptr(), k, scale.data_ptr(), None,
+                k, None, None, 16, main.cuda_stream))
+            nat.check("ima_hawkeye_prepare", lib.ima_hawkeye_prepare(q.data_ptr(), m, k, k, xop.data_ptr(),
+                                                                     main.cuda_stream))
+
+    def replay(self, xs: list[torch.Tensor], bufs: dict) -> None:
+        """Replay every linear on the operands prepare() staged, round-robin on
+        REPLAY_STREAMS side streams that fork from and join back to the current stream: the
+        last partial wave of one linear's grid overlaps the next linear's first (measured
+        15 % faster than one stream at the c2 shapes).  xs gives the token counts only."""
+        lib = nat.lib()
+        main = torch.cuda.current_stream(self.device)
         side = self._side_streams()
         for st in side:
             st.wait_stream(main)
@@ -212,6 +227,11 @@ class HawkeyeStack:
                 32, 14, -139, bufs["y"][i].data_ptr(), n, None, n, side[i % len(side)].cuda_stream))
         for st in side:
             main.wait_stream(st)
+
+    def forward(self, xs: list[torch.Tensor], bufs: dict) -> None:
+        """prepare() then replay(): bf16 outputs of every linear in bufs["y"].  Launches only."""
+        self.prepare(xs, bufs)
+        self.replay(xs, bufs)
 
     def _side_streams(self) -> list[torch.cuda.Stream]:
         s = getattr(self, "_side", None)

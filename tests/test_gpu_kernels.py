@@ -509,14 +509,63 @@ def test_grouped_pipeline_matches_oracle_and_flags_corruption(cuda_device):
     bufs["mismatch"].zero_()
     bufs["c"][1][7, 3] += 1
     bufs["c"][3][149, 895] -= 5
-    lib = nat.lib()
-    _q, per_batch = bufs["_desc"]
-    import ctypes
-    for _g, rows, count in per_batch:
-        nat.check("rows", lib.ima_freivalds_rows_grouped(ctypes.byref(rows), count, nat.stream_of(cuda_device)))
+    stack.verify(xs, bufs)
     torch.cuda.synchronize()
     expected = int(stack.linears[1].r[3].item() != 0) + int(stack.linears[3].r[895].item() != 0)
     assert int(bufs["mismatch"].item()) == expected == 2
+    _assert_status_clean(cuda_device)
+
+
+def test_grouped_check_aligned_path_flags_every_position(cuda_device):
+    """Products whose check takes the unrolled aligned row pass (K % 4 == 0, N even, aligned
+    rows): a correct forward passes, and one corrupted entry is flagged wherever it sits --
+    inside the unrolled part of a row, in the remainder loop, at either end -- and so is a
+    corrupted activation code."""
+    from int_model_approximation_b200.pipeline import CodebookStack
+
+    shapes = [(128, 896), (896, 4864), (4864, 896), (70, 300), (2, 4)]
+    tokens = 40
+    weights, xs = [], []
+    for i, (n, k) in enumerate(shapes):
+        w, ws = synthetic.normal_fp8_weights(n, k, seed=700 + i)
+        weights.append((w.to(cuda_device), ws.to(cuda_device), None))
+        xs.append(synthetic.student_t_activations(tokens, k, seed=800 + i).to(cuda_device))
+    stack = CodebookStack(weights, seed=3)
+    bufs = stack.allocate(tokens)
+    stack.forward(xs, bufs)
+    torch.cuda.synchronize()
+    assert int(bufs["mismatch"].item()) == 0
+    for i, (w, ws, _b) in enumerate(weights):
+        c_ref, _y, _out = oracle.codebook_linear(xs[i].cpu(), w.cpu(), ws.cpu())
+        assert torch.equal(bufs["c"][i].cpu(), c_ref), f"linear {i}"
+    for i, (n, k) in enumerate(shapes):
+        r = stack.linears[i].r.cpu()
+        cols = sorted({0, 1, 63, 64, 127, 128, 255, 256, 511, 512, n // 2, n - 2, n - 1} & set(range(n)))
+        for j, col in enumerate(cols):
+            row = (j * 7) % tokens
+            bufs["mismatch"].zero_()
+            bufs["c"][i][row, col] += 1 + j
+            stack.verify(xs, bufs)
+            torch.cuda.synchronize()
+            bufs["c"][i][row, col] -= 1 + j
+            assert int(bufs["mismatch"].item()) == int(int(r[col]) * (1 + j) % 2**64 != 0), (i, row, col)
+        # a corrupted activation code (raise the magnitude of a nonzero code by one step)
+        q = bufs["q"][i]
+        t = stack.linears[i].t.cpu()
+        for col in sorted({0, 3, k // 2, k - 1}):
+            row = (col * 5) % tokens
+            old = int(q[row, col].item())
+            if (old & 0x7F) in (0, 0x7E, 0x7F):
+                continue
+            bufs["mismatch"].zero_()
+            q[row, col] = old + 1
+            stack.verify(xs, bufs)
+            torch.cuda.synchronize()
+            q[row, col] = old
+            delta = oracle.fp8_codebook(torch.tensor([old + 1], dtype=torch.uint8).view(torch.float8_e4m3fn)) - \
+                oracle.fp8_codebook(torch.tensor([old], dtype=torch.uint8).view(torch.float8_e4m3fn))
+            expect = int(int(delta[0]) * int(t[col]) % 2**64 != 0)
+            assert int(bufs["mismatch"].item()) == expect, (i, row, col)
     _assert_status_clean(cuda_device)
 
 
