@@ -146,8 +146,24 @@ def lib() -> ctypes.CDLL:
                 fn = getattr(handle, name)
                 fn.restype = restype
                 fn.argtypes = argtypes
+            _check_struct_layouts(handle)
             _LIB = handle
     return _LIB
+
+
+def _check_struct_layouts(handle: ctypes.CDLL) -> None:
+    """Refuse a library whose descriptor structs differ from the ctypes mirrors above: a
+    stale build would otherwise read the grouped launches' descriptors at wrong offsets."""
+    mirrors = (QuantizeProblem, GemmProblem, FreivaldsRowsProblem)
+    sizes = (ctypes.c_int64 * len(mirrors))()
+    if handle.ima_struct_sizes(sizes, len(mirrors)) != IMA_OK:
+        raise RuntimeError(f"{_LIB_PATH}: ima_struct_sizes failed")
+    expected = [ctypes.sizeof(m) for m in mirrors]
+    if list(sizes) != expected:
+        raise RuntimeError(
+            f"{_LIB_PATH} was built from a different include/ima_b200.h: descriptor sizes {list(sizes)}, "
+            f"binding expects {expected}; rebuild with `python -m int_model_approximation_b200.build`"
+        )
 
 
 class NativeError(RuntimeError):
