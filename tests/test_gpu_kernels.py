@@ -279,6 +279,34 @@ def test_int32_raw_matmul_generic_int32(cuda_device, lo, hi):
     assert torch.equal(c.cpu(), oracle.int_gemm(a, b))
 
 
+@pytest.mark.parametrize("dtype,k", [(torch.bfloat16, 896), (torch.float32, 300), (torch.float16, 4864), (torch.float32, 1)])
+def test_int32_linear_matches_reference_forward(cuda_device, dtype, k):
+    """Int32Linear (the student the replacement pass puts on non-FP8 linears) against the CPU
+    restatement of the reference's forward: per-row / per-token int32 quantisation with
+    qmax = floor(sqrt((2^62 - 1) / K)), the exact int64 product (full-range operands, so the
+    five-plane GEMM scheme), the fp32 rescale and bias, bit for bit; one probe bump.  K = 1
+    makes qmax = 2^31 - 1, which rounds to 2^31 in fp32: the row maxima then go through
+    CUDA's saturating float -> int32 cast."""
+    g = torch.Generator().manual_seed(k)
+    n = 70
+    weight = (torch.randn(n, k, generator=g) * 0.05).to(torch.float32)
+    bias = (torch.randn(n, generator=g) * 0.1).to(torch.float32)
+    x = synthetic.student_t_activations(2 * 9, k, seed=k + 3, outlier_fraction=0.01, dtype=dtype).reshape(2, 9, k)
+    layer = students.Int32Linear(weight.to(cuda_device), bias.to(cuda_device))
+    with torch.inference_mode(), students._Int32KernelProbe() as probe:
+        y = layer(x.to(cuda_device))
+        torch.cuda.synchronize()
+    assert probe.count == 1
+    assert y.shape == (2, 9, n) and y.dtype == dtype
+    ref = oracle.int32_linear(x, weight, bias)
+    assert torch.equal(_bits_any(y.cpu()), _bits_any(ref))
+    _assert_status_clean(cuda_device)
+
+
+def _bits_any(t: torch.Tensor) -> torch.Tensor:
+    return t.contiguous().view(torch.int32 if t.dtype == torch.float32 else torch.int16)
+
+
 def test_raw_int32_matmul_is_freivalds_verifiable(cuda_device):
     """The reference's prime-matrix test (tests/test_real_integer_gemms.py:252-278)."""
     g = load_golden("freivalds")

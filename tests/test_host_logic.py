@@ -277,3 +277,20 @@ def test_codebook_stack_batches_balance_cost_within_the_launch_limit():
     assert all(len(b) <= CodebookStack.GEMM_BATCH for b in batches)
     costs = [sum(shapes[i][0] * shapes[i][1] for i in b) for b in batches]
     assert max(costs) - min(costs) <= max(n * k for n, k in shapes)
+
+
+@pytest.mark.parametrize("k", [1, 300, 896, 4864, 18944])
+def test_int32_linear_oracle_uses_the_plugin_qmax_and_tracks_the_float_product(k):
+    """The CPU restatement of Int32Linear quantises with the same qmax as the plugin's
+    `_int32_qmax` (every int32 product sum stays below 2^62), and its output is the float
+    product up to the per-token / per-row quantisation error."""
+    qmax = students._int32_qmax(k)
+    assert qmax * qmax * k <= (1 << 62) - 1
+    g = torch.Generator().manual_seed(k)
+    x = torch.randn(4, k, generator=g)
+    w = torch.randn(6, k, generator=g) * 0.05
+    y = oracle.int32_linear(x, w)
+    exact = x.double() @ w.double().t()
+    bound = (x.abs().amax(dim=1, keepdim=True).double() * w.abs().sum(dim=1).double()[None, :] / qmax
+             + w.abs().amax(dim=1).double()[None, :] * x.abs().sum(dim=1, keepdim=True).double() / qmax)
+    assert bool(((y.double() - exact).abs() <= bound + 1e-5 * exact.abs() + 1e-30).all())
