@@ -1,7 +1,7 @@
 // Per-token FP8 quantiser and the digit planes consumed by the tensor-core GEMM.
 //
 // ref: __main__.py:148-163 (_per_token_fp8, _fp8_e4m3_to_int32, _per_token_fp8_int32).
-//   scale = max(amax_k |x[m,k]| / 448, 1e-12)     fp32, IEEE division
+//   scale = max(amax_k |x[m,k]| * RN(1/448), 1e-12)   fp32 (see qz_row_scale)
 //   q     = e4m3_rne(float(x) / scale)           fp32, IEEE division, torch's e4m3fn cast
 //   code  = round(q * 512)                       exact integer, |code| <= 229376
 //
@@ -102,10 +102,22 @@ IMA_DEVINL void load8(const void* row, int dtype, int64_t k0, int64_t K, bool ve
 //
 // e4m3.  The hardware cvt.rn.satfinite.e4m3x2.f32 rounds to nearest even like
 // torch's cast; the two differ only for |f| >= 464 (torch gives NaN, satfinite
-// clamps) and NaN signs.  With a finite scale |x / s| <= 448.00003, and
+// clamps) and NaN signs.  With a finite scale |x / s| <= 448.0002, and
 // ima_quant_fast_selftest checks the two casts on every fp32 value with |f| < 464.
 // Rows with a NaN or infinite scale take the exact reference-shaped path instead.
 // ---------------------------------------------------------------------------
+// Row scale.  The reference computes `amax / FP8_E4M3_MAX` with the Python float 448.0 on
+// CUDA tensors, and torch's CUDA division kernel evaluates a tensor divided by a host scalar
+// as the tensor times the scalar's fp32 reciprocal: scale = RN(amax * RN(1/448)), then
+// clamp_min(1e-12), which keeps NaN.  (IEEE division amax / 448 gives a different fp32
+// value for about a third of the bf16 amax values; torch on the CPU divides.)
+constexpr float kQzInv448 = 0x1.24924ap-9f;   // RN(1 / 448) in fp32
+
+IMA_DEVINL float qz_row_scale(float amax) {
+    const float s = __fmul_rn(amax, kQzInv448);
+    return (s < 1e-12f) ? 1e-12f : s;
+}
+
 // (computed on |x| with x's sign restored, so that -0 / s stays -0)
 IMA_DEVINL float qz_div(float x, float s, float y) {
     const float ax = fabsf(x);
@@ -308,9 +320,7 @@ __global__ void __launch_bounds__(256, 3) quantize_rows_kernel(const __grid_cons
             amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
             has_nan |= __shfl_xor_sync(0xFFFFFFFFu, has_nan, o);
         }
-        float s = has_nan ? __int_as_float(0x7FC00000) : amax;
-        s = __fdiv_rn(s, 448.0f);
-        s = (s < 1e-12f) ? 1e-12f : s;   // clamp_min keeps NaN
+        const float s = qz_row_scale(has_nan ? __int_as_float(0x7FC00000) : amax);
         if (lane == 0) {
             P.scale[m] = s;
             if (P.code_scale) P.code_scale[m] = __fdiv_rn(s, 512.0f);
@@ -378,8 +388,7 @@ __global__ void quant_fast_selftest_kernel(int kind, unsigned long long* __restr
             const uint32_t ha = (uint32_t)(i >> 16) & 0x7FFFu, hx = (uint32_t)i & 0xFFFFu;
             const float amax = qz_half_to_f32(ha, bf16), x = qz_half_to_f32(hx, bf16);
             if (!(amax > 0.0f) || !(amax <= 3.402823466e38f) || !(fabsf(x) <= amax)) continue;
-            float s = __fdiv_rn(amax, 448.0f);
-            s = (s < 1e-12f) ? 1e-12f : s;
+            const float s = qz_row_scale(amax);
             const float y = __frcp_rn(s);
             const float fast = qz_div(x, s, y), ieee = __fdiv_rn(x, s);
             if (codes) {

@@ -6,7 +6,14 @@ Run in a container that has the reference checkout (read-only is fine):
 It imports the reference package from <checkout>/src with TRITON_INTERPRET=1, so the
 reference's own Triton kernels execute on CPU tensors, and with
 `_require_cuda_tensor` patched out exactly as the reference's tests do
-(tests/test_real_integer_gemms.py:45-46).  Hawkeye kernels are launched directly
+(tests/test_real_integer_gemms.py:45-46).  The reference only runs on CUDA tensors, where
+torch evaluates a tensor divided by a Python number as the tensor times the number's fp32
+reciprocal; torch on the CPU divides, which changes the last bit of about a third of the
+per-token scales `amax / 448.0`.  The generator therefore runs each section under
+`_CudaScalarDivision`, which applies the CUDA rule to exactly that operation (a floating
+tensor divided by a Python number) and leaves every other op to the CPU; the synthetic
+inputs drawn inside a section are stored beside the outputs, so the rule changes only which
+inputs were drawn.  Hawkeye kernels are launched directly
 with an fp32 output tensor (the interpreter truncates bf16 stores; the bf16 result is
 the RNE cast of that fp32 value, which is what a CUDA bf16 store does).  The packed
 class-count replay kernels are launched the same way (their wrappers only refuse
@@ -32,6 +39,23 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 from int_model_approximation_b200 import synthetic  # noqa: E402
+
+
+class _CudaScalarDivision(torch.overrides.TorchFunctionMode):
+    """tensor / python_number as torch computes it on CUDA tensors: RN(t * RN(1 / number)) in
+    fp32 (the op math type of fp32, bf16 and fp16), cast back to the tensor's dtype."""
+
+    DIVS = {torch.Tensor.__truediv__, torch.Tensor.div, torch.div, torch.true_divide}
+
+    def __torch_function__(self, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        if (func in self.DIVS and len(args) == 2 and not kwargs and isinstance(args[0], torch.Tensor)
+                and isinstance(args[1], (int, float)) and not isinstance(args[1], bool)
+                and args[0].dtype in (torch.float32, torch.bfloat16, torch.float16)):
+            t = args[0]
+            inv = torch.tensor(1.0, dtype=torch.float32) / torch.tensor(float(args[1]), dtype=torch.float32)
+            return (t.to(torch.float32) * inv).to(t.dtype)
+        return func(*args, **kwargs)
 
 
 def _load_reference(checkout: str):
@@ -338,7 +362,9 @@ def main() -> None:
     t0 = time.time()
     for name, fn in gens.items():
         if name in sections:
-            np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **fn())
+            with _CudaScalarDivision():
+                data = fn()
+            np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **data)
             print(f"{name}.npz written", flush=True)
     print(f"fixtures written in {time.time() - t0:.1f}s")
 

@@ -89,6 +89,24 @@ def test_quantiser_fast_path_selftest(cuda_device, kind):
     assert int(bad.item()) == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_row_scale_is_torch_cuda_division_for_every_amax(cuda_device, dtype):
+    """The reference forms the row scale as `amax / 448.0` on CUDA tensors, where torch
+    multiplies by the fp32 reciprocal.  One row per positive finite value of the dtype (the
+    row's amax) plus smaller elements: the kernel's scale equals torch's CUDA expression, and
+    the oracle's CPU emulation of that rule, bit for bit."""
+    bits = torch.arange(1, 0x7C00 if dtype == torch.float16 else 0x7F80, dtype=torch.int32).to(torch.int16)
+    amax = bits.view(dtype)
+    x = torch.stack([amax, -amax * 0.5, amax * 0.25, torch.zeros_like(amax)], dim=1).repeat(1, 4)
+    xd = x.to(cuda_device)
+    _q, scale, *_ = codebook.per_token_fp8(xd)
+    expect = (xd.abs().amax(dim=1, keepdim=True).to(torch.float32) / 448.0).clamp_min(1e-12)
+    assert torch.equal(scale.reshape(-1).view(torch.int32), expect.reshape(-1).view(torch.int32))
+    _q_ref, s_ref = oracle.per_token_fp8(x)
+    assert torch.equal(s_ref.reshape(-1).view(torch.int32), expect.reshape(-1).cpu().view(torch.int32))
+    assert int((expect.reshape(-1).cpu() != x.abs().amax(dim=1).float() / 448.0).sum()) > 0   # the rules differ
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_quantiser_special_rows_and_planes(cuda_device, dtype):
     """Rows with NaN, +-inf, all zeros, tiny (subnormal) values and a ragged K.  Codes are
@@ -111,6 +129,8 @@ def test_quantiser_special_rows_and_planes(cuda_device, dtype):
     s_cuda = (xd.float().abs().amax(dim=1, keepdim=True) / 448.0).clamp_min(1e-12)
     q_cuda = (xd.float() / s_cuda).to(torch.float8_e4m3fn)
     assert torch.equal(q.view(torch.uint8), q_cuda.view(torch.uint8))
+    finite = torch.isfinite(s_cuda.reshape(-1))
+    assert torch.equal(scale.reshape(-1)[finite].view(torch.int32), s_cuda.reshape(-1)[finite].view(torch.int32))
     q_ref, s_ref = oracle.per_token_fp8(x)
     unsigned_nan = (q.view(torch.uint8).cpu() & 0x7F) == 0x7F
     assert torch.equal(unsigned_nan, (q_ref.view(torch.uint8) & 0x7F) == 0x7F)
