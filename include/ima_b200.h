@@ -53,7 +53,7 @@ int ima_int32_issue_probe(int64_t iters, int blocks, uint32_t* sink, void* strea
  * *mismatches (device memory, zeroed by the caller) the number of disagreements:
  * kind 0 - the hardware e4m3 cast vs the torch-shaped software cast on every fp32
  * value with |f| < 464; kind 1 / 2 - for every positive finite bf16 / fp16 amax
- * (s = max(amax/448, 1e-12)) and every bf16 / fp16 element x with |x| <= amax, the e4m3
+ * (s = max(amax * RN(1/448), 1e-12)) and every bf16 / fp16 element x with |x| <= amax, the e4m3
  * code of the corrected-reciprocal quotient vs the code of the IEEE quotient x / s;
  * kind 3 / 4 - the same pairs, the fp32 quotients themselves wherever x / s is a normal
  * number and |x| >= 2^-100 (no underflow in the correction step).  A correct build
@@ -82,7 +82,8 @@ int ima_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
  *      :161-163 _per_token_fp8_int32.
  * x [M,K] (dtype IMA_DTYPE_*, row stride ldx) ->
  *   q_fp8 [M,K] e4m3 bytes (row stride ldq),
- *   scale [M] fp32 = max(amax_row|x| / 448, 1e-12),
+ *   scale [M] fp32 = max(amax_row|x| * RN(1/448), 1e-12): the reference's amax / 448.0 as
+ *     torch evaluates it on CUDA tensors (multiplication by the fp32 reciprocal),
  *   codebook [M,K] int32 = round(q * 512) (optional, row stride ldc),
  *   code_scale [M] fp32 = scale / 512 (optional),
  *   planes [3][M][ldp] int8: the three balanced base-128 digit planes of the codebook

@@ -54,7 +54,8 @@ def per_token_fp8(x: torch.Tensor, *, codebook: bool = False, planes: bool = Fal
 
     Returns (q_fp8 [M,K], scale [M,1] fp32, codebook int32 [M,K] or None,
     code_scale [M,1] or None, DigitPlanes or None).  Bit-identical to the
-    reference's torch expression (amax / 448, clamp 1e-12, fp32 division, e4m3 RNE).
+    reference's torch expression as it runs on CUDA (amax / 448 as a multiplication by the
+    fp32 reciprocal, clamp 1e-12, fp32 division of the elements, e4m3 RNE).
     """
     _require_cuda(x, "FP8 activation")
     rows = x.reshape(-1, x.shape[-1])

@@ -4,7 +4,8 @@ Activations: Student-t(nu=4) * 0.5, drawn as z / sqrt(chi2_4 / 4) with
 chi2_4 = -2 log(u1 u2), optionally with a fraction of entries scaled by 50 as
 outliers, rounded to bf16.  Weights: N(0, 0.02) quantised per output channel to
 e4m3 with scale = max(amax / 448, 1e-12) (the activation quantiser's formula applied
-per row), weight_scale [N, 1] fp32.  Every tensor is drawn from its own
+per row, evaluated by torch on the generator's device: on CUDA the division by 448 is a
+multiplication by its fp32 reciprocal), weight_scale [N, 1] fp32.  Every tensor is drawn from its own
 torch.Generator seeded with `seed`, on the device the generator lives on; the GPU
 kernels and the CPU oracle are always fed the same materialised bytes.
 """
