@@ -327,6 +327,72 @@ def _bits_any(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous().view(torch.int32 if t.dtype == torch.float32 else torch.int16)
 
 
+def _ref_test_fp8_weight(device) -> torch.Tensor:
+    """The hand-written FP8 weight of the reference's integer-GEMM tests."""
+    return torch.tensor([[0.125, -0.5, 1.0], [-1.5, 0.25, 2.0], [3.0, -0.75, 0.5], [-2.5, 1.5, -0.125]],
+                        dtype=torch.float32, device=device).to(torch.float8_e4m3fn)
+
+
+def test_codebook_linear_uses_one_int32_matmul_path(cuda_device, monkeypatch):
+    """CodebookLinear.forward makes exactly one int32 x int32 matmul call and no float GEMM."""
+    layer = students.CodebookLinear(_ref_test_fp8_weight(cuda_device), torch.ones(4, 1, device=cuda_device), None)
+    calls = []
+
+    def fake_int32_matmul(activations, weight_t, x_scale, w_scale):
+        calls.append((activations, weight_t, x_scale, w_scale))
+        assert activations.dtype == torch.int32 and weight_t.dtype == torch.int32
+        return torch.zeros((activations.shape[0], weight_t.shape[1]), dtype=torch.float32, device=activations.device)
+
+    monkeypatch.setattr(students, "_int32_matmul", fake_int32_matmul)
+
+    def fail(*_args, **_kwargs):
+        raise AssertionError("the codebook student used a float GEMM")
+
+    for attr in ("mm", "matmul", "addmm", "bmm", "_scaled_mm"):
+        monkeypatch.setattr(torch, attr, fail)
+    monkeypatch.setattr(torch.nn.functional, "linear", fail)
+    y = layer(torch.randn(2, 3, device=cuda_device))
+    assert len(calls) == 1
+    assert y.shape == (2, 4)
+
+
+def test_forward_integer_gemms_are_freivalds_verifiable(cuda_device, monkeypatch):
+    """Every integer product of an integerised forward, captured at the matmul boundary, is
+    exact (against the oracle) and passes the Freivalds check with the reference test's
+    vectors; a corrupted product fails it."""
+    linear = torch.nn.Linear(3, 4, bias=False, device=cuda_device)
+    linear.weight = torch.nn.Parameter(_ref_test_fp8_weight(cuda_device), requires_grad=False)
+    linear.weight_scale = torch.ones(4, 1, device=cuda_device)
+    model = torch.nn.Sequential(linear)
+    monkeypatch.setattr(students, "STUDENT_KERNEL", "codebook")
+    students._replace_int32_linears(model)
+    assert isinstance(model[0], students.CodebookLinear)
+    captured = []
+    original = students._int32_matmul
+
+    def wrapped(activations, weight_t, x_scale, w_scale):
+        captured.append((activations.detach().clone(), weight_t.detach().clone()))
+        return original(activations, weight_t, x_scale, w_scale)
+
+    monkeypatch.setattr(students, "_int32_matmul", wrapped)
+    x = torch.tensor([[0.25, -1.5, 2.0], [3.0, -0.75, 0.125]], device=cuda_device)
+    with torch.inference_mode():
+        y = model(x)
+        torch.cuda.synchronize()
+    assert y.device.type == "cuda" and len(captured) == 1
+    for a, b in captured:
+        c = students._int32_raw_matmul(a, b)
+        assert torch.equal(c.cpu(), oracle.int_gemm(a.cpu(), b.cpu()))
+        n = b.shape[1]
+        for vec in ([1] + [0] * (n - 1), [1 if i % 2 == 0 else -1 for i in range(n)],
+                    [0 if i % 3 == 0 else 1 for i in range(n)]):
+            r = torch.tensor(vec, dtype=torch.int64, device=cuda_device)
+            assert freivalds.verify_int32_product(a, b, c, r)
+        bad = c.clone()
+        bad[1, 0] += 1
+        assert not freivalds.verify_int32_product(a, b, bad, torch.ones(n, dtype=torch.int64, device=cuda_device))
+
+
 def test_raw_int32_matmul_is_freivalds_verifiable(cuda_device):
     """The reference's prime-matrix test (tests/test_real_integer_gemms.py:252-278)."""
     g = load_golden("freivalds")

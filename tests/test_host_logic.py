@@ -294,3 +294,55 @@ def test_int32_linear_oracle_uses_the_plugin_qmax_and_tracks_the_float_product(k
     bound = (x.abs().amax(dim=1, keepdim=True).double() * w.abs().sum(dim=1).double()[None, :] / qmax
              + w.abs().amax(dim=1).double()[None, :] * x.abs().sum(dim=1, keepdim=True).double() / qmax)
     assert bool(((y.double() - exact).abs() <= bound + 1e-5 * exact.abs() + 1e-30).all())
+
+
+def _call_name(node) -> str | None:
+    import ast
+
+    if isinstance(node, ast.Name):
+        return node.id
+    if isinstance(node, ast.Attribute):
+        base = _call_name(node.value)
+        return f"{base}.{node.attr}" if base else node.attr
+    return None
+
+
+def _named_source(module, name: str) -> str:
+    import ast
+    import inspect
+
+    source = inspect.getsource(module)
+    for node in ast.parse(source).body:
+        if isinstance(node, (ast.ClassDef, ast.FunctionDef)) and node.name == name:
+            return ast.get_source_segment(source, node) or ""
+    raise AssertionError(f"{name} not found in {module.__name__}")
+
+
+def test_int32_path_source_has_no_float_gemm_or_cpu_fallbacks():
+    """The integer students and the GEMM wrapper they call use no float GEMM, no CPU copy and
+    no fake-quantisation path (the reference's own source check of its int32 path), and the
+    product reaches the native library."""
+    import ast
+
+    from int_model_approximation_b200 import codebook
+
+    source = "\n".join([
+        _named_source(students, "Int32Linear"),
+        _named_source(students, "CodebookLinear"),
+        _named_source(students, "_int32_raw_matmul"),
+        _named_source(students, "_int32_matmul"),
+        _named_source(students, "_operand_planes"),
+        _named_source(codebook, "int_gemm"),
+    ])
+    calls = {name for node in ast.walk(ast.parse(source)) if isinstance(node, ast.Call)
+             for name in [_call_name(node.func)] if name}
+    forbidden_calls = {"torch._scaled_mm", "torch.addmm", "torch.baddbmm", "torch.bmm", "torch.matmul", "torch.mm",
+                       "torch.nn.functional.linear", "F.linear", "torch._int_mm"}
+    assert calls.isdisjoint(forbidden_calls), calls & forbidden_calls
+    code_only = "\n".join(line.split("#", 1)[0] for line in source.splitlines())
+    for text in (".cpu(", "device='cpu'", 'device="cpu"', "fake_quant", "FakeQuantize", "QuantStub",
+                 "DeQuantStub", "torch.ops.quantized"):
+        assert text not in code_only, text
+    assert not any(isinstance(node, ast.BinOp) and isinstance(node.op, ast.MatMult)
+                   for node in ast.walk(ast.parse(source)))   # no `a @ b` on the path
+    assert "ima_int_gemm" in _named_source(codebook, "int_gemm")
