@@ -210,3 +210,9 @@ void oracle_int_gemm_nk(const int32_t *a, const int32_t *bnk, int M, int N, int 
         }
     }
 }
+
+/* hawkeye_freivalds.py:120-144 over arrays (for the gfloat known-answer checks). */
+void oracle_gfloat_to_float32(const int32_t *sign, const int64_t *exponent, const int64_t *significand, int n,
+                              float *out) {
+    for (int i = 0; i < n; ++i) out[i] = gfloat_to_float32(sign[i], exponent[i], significand[i]);
+}

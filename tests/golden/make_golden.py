@@ -311,6 +311,21 @@ def gen_class_counts(hf) -> dict:
     return out
 
 
+def gen_gfloat(hf) -> dict:
+    """The reference's gfloat -> fp32 conversion (hawkeye_freivalds.py:120-144) over every
+    exponent from -170 to 149, both signs, and structured plus random significands."""
+    sigs = [0, 1, 2, 3, 0x3FFF, 0x4000, 0x2000 << 10, 0x3FFF << 10, 0x7FFFFF, 0x800000, 0x800001, 0xFFFFFF,
+            0x1000000, 0x1FFFFFF, 1 << 40, (1 << 62) - 1]
+    g = torch.Generator().manual_seed(71)
+    sigs += torch.randint(0, 1 << 24, (24,), generator=g).tolist()
+    sign, exp, sig = torch.meshgrid(torch.tensor([0, 1]), torch.arange(-170, 150), torch.tensor(sigs, dtype=torch.int64),
+                                    indexing="ij")
+    sign, exp, sig = sign.reshape(-1), exp.reshape(-1).to(torch.int64), sig.reshape(-1)
+    y = hf._gfloat_to_float32(sign.to(torch.bool), exp, sig)
+    return dict(sign=sign.to(torch.int8).numpy(), exponent=exp.numpy(), significand=sig.numpy(),
+                f32_bits=y.to(torch.float32).view(torch.int32).numpy())
+
+
 def _test_matrices(checkout: str) -> tuple[list, list]:
     """The prime matrices of the reference's Freivalds test, read from its source."""
     path = os.path.join(checkout, "tests", "test_real_integer_gemms.py")
@@ -350,7 +365,8 @@ def main() -> None:
     if not checkout or not os.path.isdir(checkout):
         raise SystemExit("usage: make_golden.py <reference checkout>")
     entry, hk, hf = _load_reference(checkout)
-    sections = set(sys.argv[2:]) or {"quantize", "e4m3_cast", "codebook", "freivalds", "hawkeye", "class_counts"}
+    sections = set(sys.argv[2:]) or {"quantize", "e4m3_cast", "codebook", "freivalds", "hawkeye", "class_counts",
+                                     "gfloat"}
     gens = {
         "quantize": lambda: gen_quantize(entry),
         "e4m3_cast": gen_e4m3_cast,
@@ -358,6 +374,7 @@ def main() -> None:
         "freivalds": lambda: gen_freivalds(entry, checkout),
         "hawkeye": lambda: gen_hawkeye(hk, hf),
         "class_counts": lambda: gen_class_counts(hf),
+        "gfloat": lambda: gen_gfloat(hf),
     }
     t0 = time.time()
     for name, fn in gens.items():

@@ -174,3 +174,23 @@ def test_digit_shift_recombination_is_exact(count, lo, hi):
         for j in range(count):
             c = c + (da[i].astype(object) @ db[j].T.astype(object)) * (2 ** (7 * (i + j)))
     assert np.array_equal(c, a.astype(object) @ b.T.astype(object))
+
+
+def test_gfloat_known_answers_of_the_reference_tests():
+    """tests/test_hawkeye_freivalds.py:28-46 of the reference, against the oracle's gfloat
+    conversion: a zero significand is +0, and the smallest nonzero one at the zero exponent
+    stays a tiny finite value instead of wrapping to a large one."""
+    zero = oracle.gfloat_to_float32(torch.tensor([False]), torch.tensor([-139]), torch.tensor([0]))
+    assert zero.item() == 0.0
+    tiny = oracle.gfloat_to_float32(torch.tensor([False]), torch.tensor([-139]), torch.tensor([1]))
+    assert torch.isfinite(tiny).all() and tiny.abs().item() < 1e-35
+
+
+def test_gfloat_conversion_matches_reference_sweep():
+    """The oracle's gfloat -> fp32 conversion equals the reference's on every exponent from
+    -170 to 149, both signs, structured and random significands (fixture made by the
+    reference's own function)."""
+    g = load_golden("gfloat")
+    y = oracle.gfloat_to_float32(torch.from_numpy(g["sign"].astype(np.int32)), torch.from_numpy(g["exponent"]),
+                                 torch.from_numpy(g["significand"]))
+    assert np.array_equal(y.numpy().view(np.int32), g["f32_bits"])
