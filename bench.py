@@ -557,33 +557,39 @@ def run_b200(args) -> None:
 def cpu_baseline_sample(shapes, weights, xs, budget_s: float = 15.0) -> dict:
     """The reference's CPU path (oracle port: torch quantiser, torch int64 matmul,
     fp32 rescale) on a bounded sample of the same workload: whole linears, cycling
-    through the model, until the time budget is used."""
+    through the model, until the time budget is used.  torch's int64 matmul is
+    single-threaded, so each linear's token rows are split over all host threads; the
+    weight codes are prepared once per linear outside the timed region, as the
+    reference's CodebookLinear.__init__ does."""
     import oracle
 
     threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+    prev_threads = torch.get_num_threads()
+    torch.set_num_threads(1)   # one row part per host thread instead of intra-op threads
     done_ops, t_used, linears = 0.0, 0.0, 0
-    cpu_w = {}
     i = 0
-    while t_used < budget_s and linears < len(shapes):
-        s = shapes[i]
-        w, ws, bias = weights[i]
-        if i not in cpu_w:
-            cpu_w[i] = (w.cpu(), ws.cpu(), bias.cpu())
-        x = xs[i].cpu()
-        wc, wsc, bc = cpu_w[i]
-        t0 = time.perf_counter()
-        oracle.torch_cpu_codebook_linear(x, wc, wsc, bc)
-        t_used += time.perf_counter() - t0
-        done_ops += 2.0 * x.shape[0] * s.n * s.k
-        linears += 1
-        i += 1
+    try:
+        while t_used < budget_s and linears < len(shapes):
+            s = shapes[i]
+            w, ws, bias = weights[i]
+            wc, wsc, bc = w.cpu(), ws.cpu(), bias.cpu()
+            codes = oracle.fp8_codebook(wc).to(torch.int64)
+            x = xs[i].cpu()
+            t0 = time.perf_counter()
+            oracle.torch_cpu_codebook_linear(x, wc, wsc, bc, threads=threads, w_codes=codes)
+            t_used += time.perf_counter() - t0
+            done_ops += 2.0 * x.shape[0] * s.n * s.k
+            linears += 1
+            i += 1
+    finally:
+        torch.set_num_threads(prev_threads)
     return {
         "value": round(done_ops / t_used / 1e12, 6),
         "unit": "TOPS",
         "cores": threads,
         "kind": "port",
-        "sample": f"{linears} whole linears of the c1 workload ({TOKENS} tokens each), {t_used:.1f} s of CPU time",
+        "sample": f"{linears} whole linears of the c1 workload ({TOKENS} tokens each, rows split over "
+                  f"{threads} threads), {t_used:.1f} s",
     }
 
 
@@ -595,7 +601,7 @@ def run_reference(args) -> None:
     import oracle
 
     threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+    torch.set_num_threads(1)   # one row part per host thread (torch's int64 matmul is single-threaded)
     shapes = synthetic.config_linears(1)
     rows = args.reference_rows
 
@@ -604,16 +610,16 @@ def run_reference(args) -> None:
         seed = synthetic.linear_seed(1, i % len(shapes))
         x = synthetic.student_t_activations(rows, s.k, seed)
         w, ws = synthetic.normal_fp8_weights(s.n, s.k, seed + 500_000)
-        return s, x, w, ws
+        return s, x, w, ws, oracle.fp8_codebook(w).to(torch.int64)   # weight prepack: once per linear
 
     for i in range(args.warmup):
-        s, x, w, ws = sample(i)
-        oracle.torch_cpu_codebook_linear(x, w, ws, None)
+        s, x, w, ws, codes = sample(i)
+        oracle.torch_cpu_codebook_linear(x, w, ws, None, threads=threads, w_codes=codes)
     total_t, total_ops = 0.0, 0.0
     for i in range(args.steps):
-        s, x, w, ws = sample(args.warmup + i)
+        s, x, w, ws, codes = sample(args.warmup + i)
         t0 = time.perf_counter()
-        oracle.torch_cpu_codebook_linear(x, w, ws, None)
+        oracle.torch_cpu_codebook_linear(x, w, ws, None, threads=threads, w_codes=codes)
         total_t += time.perf_counter() - t0
         total_ops += 2.0 * rows * s.n * s.k
     value = total_ops / total_t / 1e12
@@ -632,9 +638,11 @@ def run_reference(args) -> None:
         "dtype": "int64",
         "data": "synthetic",
         "config": {"workload": "c1: 168 FP8 linears of Qwen2.5-0.5B shape, codebook student",
-                   "sample_rows_per_step": rows},
+                   "sample_rows_per_step": rows,
+                   "freivalds": "not timed: the reference checks its products only in its tests"},
         "cpu_baseline": {"value": round(value, 6), "unit": "TOPS", "cores": threads, "kind": "port",
-                         "sample": f"one linear per step, {rows} token rows, cycling through the 168 linears"},
+                         "sample": f"one whole linear per step ({rows} token rows, as in the workload, split "
+                                   f"over {threads} threads), cycling through the 168 linears"},
         "e2e": {"value": round(value, 6), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -889,7 +897,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--reference-rows", type=int, default=64)
+    ap.add_argument("--reference-rows", type=int, default=TOKENS)
     ap.add_argument("--profile-step", action="store_true", help="two eager forwards only (for ncu)")
     ap.add_argument("--profile-tokens", type=int, default=TOKENS)
     ap.add_argument("--hawkeye-only", action="store_true", help="only the config-2 Hawkeye measurement")
