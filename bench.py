@@ -247,9 +247,45 @@ def run_hawkeye(args, emit: bool = True) -> dict:
         },
         "launches_per_step": stack.launches_per_forward(),
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = hawkeye_cpu_baseline(shapes, stack, bufs, budget_s=args.hawkeye_cpu_seconds)
     if emit and rank == 0:
         print(json.dumps({"hawkeye": res}), flush=True)
     return res
+
+
+def hawkeye_cpu_baseline(shapes, stack, bufs, budget_s: float) -> dict:
+    """The replay on the host cores: the oracle's scalar C restatement of the reference's
+    Hawkeye kernel (hawkeye.py:127-219; the reference's own CPU form, exact_hawkeye_fp8_sum
+    with a CPU raw_matmul, needs about 160 s per K = 32 group of one c0 row block), its rows
+    split over the host threads.  Bounded sample: 64 token rows of each linear in turn,
+    quantised by the GPU step above, until the budget is used."""
+    import oracle
+
+    rows = 64
+    done_products, done_outputs, t_used, linears = 0.0, 0.0, 0.0, 0
+    while t_used < budget_s and linears < len(shapes):
+        i = linears
+        s = shapes[i]
+        w, ws = stack.weights[i]
+        xq = bufs["q"][i][:rows].cpu().view(torch.float8_e4m3fn)
+        xs = bufs["scale"][i][:rows].cpu()
+        wq, wsc = w.cpu(), ws.cpu()
+        t0 = time.perf_counter()
+        oracle.hawkeye(xq, xs, wq, wsc)
+        t_used += time.perf_counter() - t0
+        done_products += float(rows) * s.n * s.k
+        done_outputs += float(rows) * s.n
+        linears += 1
+    threads = max(1, min(32, os.cpu_count() or 1))
+    return {
+        "value": done_products / t_used,
+        "unit": "products/s",
+        "outputs_per_s": done_outputs / t_used,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{rows} token rows of each of the first {linears} linears, {t_used:.1f} s",
+    }
 
 
 def run_profile_step(args) -> None:
@@ -897,6 +933,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--hawkeye-cpu-seconds", type=float, default=8.0)
     ap.add_argument("--reference-rows", type=int, default=TOKENS)
     ap.add_argument("--profile-step", action="store_true", help="two eager forwards only (for ncu)")
     ap.add_argument("--profile-tokens", type=int, default=TOKENS)
