@@ -447,7 +447,6 @@ def exact_hawkeye_fp8_sum(
     _validate_params(products_per_group, internal_width, zero_exponent)
 
     m_size, k_size = x_fp8.shape
-    n_size = w_fp8.shape[0]
     # The reference scales with y * x_scale * w_scale.reshape(1, -1), x_scale being the
     # per-token [M, 1] scale; a scalar scale broadcasts the same way.
     if x_scale.numel() not in (1, m_size):

@@ -200,7 +200,7 @@ class HawkeyeStack:
         """Quantise and stage every activation xs[i] [tokens, K_i] (two launches per linear)."""
         lib = nat.lib()
         main = torch.cuda.current_stream(self.device)
-        for i, (w, _ws) in enumerate(self.weights):
+        for i in range(len(self.weights)):
             x = xs[i]
             m, k = int(x.shape[0]), int(x.shape[1])
             q, scale, xop = bufs["q"][i], bufs["scale"][i], bufs["xop"][i]
