@@ -254,6 +254,71 @@ def run_hawkeye(args, emit: bool = True) -> dict:
     return res
 
 
+def run_class_counts_c3(args) -> dict:
+    """Config 3: the hawkeye-class-counts student on the down_proj shape (M = 4096, K = 4864,
+    N = 896) with class_chunk 512, 6 packed count lanes and 2 packed group lanes, through
+    exact_hawkeye_fp8_sum with this package's _int32_raw_matmul (what
+    HawkeyeClassCountsLinear passes): the per-pack class presence for the stats, then the
+    output from the direct replay.  Each call reads the stats back to the host (as the
+    reference's does), so each timed call is bracketed by CUDA events on an otherwise idle
+    stream.  The output is compared with the direct replay once, outside the timing."""
+    from int_model_approximation_b200 import codebook, hawkeye, hawkeye_freivalds, students, synthetic
+
+    device = torch.device("cuda", 0)
+    shape = synthetic.LinearShape("down_proj", 896, 4864)
+    x, w, ws = synthetic.make_linear_inputs(3, 0, shape, device=device)
+    xq, xs, *_ = codebook.per_token_fp8(x)
+    params = dict(class_chunk=512, packed_count_lanes=6, packed_group_lanes=2)
+
+    def call():
+        return hawkeye_freivalds.exact_hawkeye_fp8_sum(xq, xs, w, ws, students._int32_raw_matmul, **params)
+
+    y, stats = call()
+    direct, _ = hawkeye.hawkeye_fp8_sum(xq, xs, w, ws)
+    equal = bool(torch.equal(y.view(torch.int16), direct.view(torch.int16)))
+    for _ in range(2):
+        call()
+    torch.cuda.synchronize()
+    steps = 5
+    total_ms = 0.0
+    stream = torch.cuda.current_stream(device)
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        call()
+        b.record(stream)
+        b.synchronize()
+        total_ms += a.elapsed_time(b)
+    ms = total_ms / steps
+    m, n, k = int(x.shape[0]), shape.n, shape.k
+    res = {
+        "workload": "c3: down_proj 4096 x 4864 -> 896, hawkeye-class-counts, class_chunk 512, "
+                    "6 count lanes, 2 group lanes",
+        "outputs_per_s": m * n / (ms * 1e-3),
+        "products_per_s": m * n * k / (ms * 1e-3),
+        "ms_per_call": round(ms, 4),
+        "steps": steps,
+        "equals_direct_replay": equal,
+        "stats": {key: val for key, val in stats.__dict__.items()},
+        "note": "the checkable count products are folded into the replay, not formed: "
+                "total_checkable_products is the number the reference would send through its int GEMM",
+    }
+    if not args.no_cpu_baseline:
+        import oracle
+
+        rows = 128
+        t0 = time.perf_counter()
+        oracle.hawkeye(xq[:rows].cpu(), xs[:rows].cpu(), w.cpu(), ws.cpu())
+        t = time.perf_counter() - t0
+        res["cpu_baseline"] = {
+            "value": rows * n * k / t, "unit": "products/s", "cores": max(1, min(32, os.cpu_count() or 1)),
+            "kind": "port",
+            "sample": f"{rows} token rows through the oracle's C restatement of the replay (the output equals "
+                      f"the direct replay), {t:.1f} s",
+        }
+    return res
+
+
 def hawkeye_cpu_baseline(shapes, stack, bufs, budget_s: float) -> dict:
     """The replay on the host cores: the oracle's scalar C restatement of the reference's
     Hawkeye kernel (hawkeye.py:127-219; the reference's own CPU form, exact_hawkeye_fp8_sum
@@ -584,6 +649,11 @@ def run_b200(args) -> None:
                 line["hawkeye_c2"] = run_hawkeye(args, emit=False)
             except Exception as exc:  # noqa: BLE001
                 line["hawkeye_c2"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        if world == 1 and not args.no_class_counts:
+            try:
+                line["class_counts_c3"] = run_class_counts_c3(args)
+            except Exception as exc:  # noqa: BLE001
+                line["class_counts_c3"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         print(json.dumps(line), flush=True)
     if world > 1:
         del graph, phase_graphs
@@ -934,6 +1004,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--hawkeye-cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-class-counts", action="store_true")
     ap.add_argument("--reference-rows", type=int, default=TOKENS)
     ap.add_argument("--profile-step", action="store_true", help="two eager forwards only (for ncu)")
     ap.add_argument("--profile-tokens", type=int, default=TOKENS)
