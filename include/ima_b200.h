@@ -210,7 +210,10 @@ int ima_freivalds_weight_vector(const uint8_t* w_fp8, int64_t ldw, const int64_t
 
 /* The row half for many products in one launch: for each problem, adds to
  * *mismatch_rows the rows m with A[m,:] . t != C[m,:] . r (mod 2^64).  A is e4m3 codes
- * (a_kind IMA_FREIVALDS_A_FP8, checked through their codebook values) or int32. */
+ * (a_kind IMA_FREIVALDS_A_FP8, checked through their codebook values) or int32.  Up to
+ * 192 problems go into one launch (more are split).  A launch whose problems are all fp8
+ * with K a multiple of 4, N even, 4-byte aligned code rows and 16-byte aligned C rows, t
+ * and r takes the faster unrolled path; any other launch the general one (same result). */
 #define IMA_FREIVALDS_A_FP8 0
 #define IMA_FREIVALDS_A_INT32 1
 typedef struct ima_freivalds_rows_problem {
