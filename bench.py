@@ -37,6 +37,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 TOKENS = 512
+# the metric both arms report (the driver compares the lines)
+METRIC = "exact int GEMM TOPS (bit-exact codebook int64 GEMM + fused rescale + Freivalds check)"
 
 
 def _dist():
@@ -564,7 +566,7 @@ def run_b200(args) -> None:
         gemm_tc_ops = 9.0 * flops / (gemm_ms_per_step * 1e-3) / 1e12
         traffic = profile_traffic("int_gemm_c1")
         line = {
-            "metric": "exact int GEMM TOPS (bit-exact codebook int64 GEMM + fused rescale + Freivalds check)",
+            "metric": METRIC,
             "value": round(value, 3),
             "unit": "TOPS",
             "n_gpus": world,
@@ -731,7 +733,7 @@ def run_reference(args) -> None:
     value = total_ops / total_t / 1e12
     line = {
         "impl": "reference",
-        "metric": "exact int GEMM TOPS (bit-exact codebook int64 GEMM + fused rescale + Freivalds check)",
+        "metric": METRIC,
         "value": round(value, 6),
         "unit": "TOPS",
         "n_gpus": world,
