@@ -351,8 +351,9 @@ constexpr int FV_NOALLOC_MAX_DEVICES = 64;
 std::mutex g_fv_noalloc_mutex;
 unsigned long long* g_fv_noalloc_ptr[FV_NOALLOC_MAX_DEVICES] = {};
 
-// Device address of the scratch array on the current device (looked up on first use).
-int fv_noalloc_scratch(unsigned long long** out) {
+// Device address of the scratch array on the current device (looked up on first use);
+// *dev_out receives that device.
+int fv_noalloc_scratch(unsigned long long** out, int* dev_out) {
     int dev = -1;
     int rc = ima_note_cuda(cudaGetDevice(&dev));
     if (rc != IMA_OK) return rc;
@@ -366,6 +367,30 @@ int fv_noalloc_scratch(unsigned long long** out) {
         g_fv_noalloc_ptr[dev] = reinterpret_cast<unsigned long long*>(p);
     }
     *out = g_fv_noalloc_ptr[dev];
+    *dev_out = dev;
+    return IMA_OK;
+}
+
+// The scratch array used is the current device's copy, so the stream and every operand
+// must belong to that device: a stream of another GPU would run the kernels there against
+// this GPU's array, and a host or other-GPU pointer would reach a kernel.  Checked before
+// any launch; a mismatch is IMA_ERR_INVALID_ARGUMENT.
+int fv_noalloc_same_device(int dev, cudaStream_t s, const void* const* ptrs, int n) {
+    int sdev = -1;
+    if (cudaStreamGetDevice(s, &sdev) != cudaSuccess) {
+        cudaGetLastError();
+        return IMA_ERR_INVALID_ARGUMENT;
+    }
+    if (sdev != dev) return IMA_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < n; ++i) {
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, ptrs[i]) != cudaSuccess) {
+            cudaGetLastError();
+            return IMA_ERR_INVALID_ARGUMENT;
+        }
+        if (a.type == cudaMemoryTypeManaged) continue;
+        if (a.type != cudaMemoryTypeDevice || a.device != dev) return IMA_ERR_INVALID_ARGUMENT;
+    }
     return IMA_OK;
 }
 
@@ -378,7 +403,11 @@ extern "C" int ima_freivalds_fp8_noalloc(const uint8_t* x_fp8, int64_t ldx, cons
     if (M < 0 || N < 0 || K < 0 || ldx < K || ldw < K || ldc < N) return IMA_ERR_INVALID_ARGUMENT;
     if (K > IMA_FREIVALDS_NOALLOC_MAX_K) return IMA_ERR_UNSUPPORTED;   // the fixed scratch holds K <= max
     unsigned long long* scratch = nullptr;
-    int rc = fv_noalloc_scratch(&scratch);
+    int dev = -1;
+    int rc = fv_noalloc_scratch(&scratch, &dev);
+    if (rc != IMA_OK) return rc;
+    const void* operands[5] = {x_fp8, w_fp8, c, r, mismatch_rows};
+    rc = fv_noalloc_same_device(dev, (cudaStream_t)stream, operands, 5);
     if (rc != IMA_OK) return rc;
     return ima_freivalds_fp8(x_fp8, ldx, w_fp8, ldw, c, ldc, r, M, N, K, scratch, mismatch_rows, stream);
 }

@@ -70,6 +70,54 @@ def test_noalloc_freivalds_matches_the_allocating_check_on_two_calls(cuda_device
     assert _noalloc(q2, w2, c2, r2) == _allocating(q2, w2, c2, r2) == 1
 
 
+def test_noalloc_freivalds_on_two_streams_ordered_by_an_event(cuda_device):
+    """Two calls on different streams, the second ordered after the first by an event, agree
+    with the allocating check (the shared array is cleared by each call)."""
+    q, w, c, r = _product(cuda_device, 64, 896, 130, seed=13)
+    bad = c.clone()
+    bad[10, 5] += 2
+    outs = [torch.zeros((1,), dtype=torch.int32, device=cuda_device) for _ in range(2)]
+    s1, s2 = torch.cuda.Stream(cuda_device), torch.cuda.Stream(cuda_device)
+    s1.wait_stream(torch.cuda.current_stream(cuda_device))
+    m, k = q.shape
+    n = w.shape[0]
+    with torch.cuda.stream(s1):
+        nat.call("ima_freivalds_fp8_noalloc", q.data_ptr(), k, w.data_ptr(), k, bad.data_ptr(), n, r.data_ptr(), m,
+                 n, k, outs[0].data_ptr(), s1.cuda_stream)
+    done = torch.cuda.Event()
+    done.record(s1)
+    s2.wait_event(done)
+    with torch.cuda.stream(s2):
+        nat.call("ima_freivalds_fp8_noalloc", q.data_ptr(), k, w.data_ptr(), k, c.data_ptr(), n, r.data_ptr(), m,
+                 n, k, outs[1].data_ptr(), s2.cuda_stream)
+    torch.cuda.synchronize(cuda_device)
+    assert int(outs[0].item()) == _allocating(q, w, bad, r) == int(r[5].item() != 0)
+    assert int(outs[1].item()) == _allocating(q, w, c, r) == 0
+
+
+def test_noalloc_freivalds_refuses_operands_off_the_current_device(cuda_device):
+    """A host pointer among the operands is refused before any launch (the call would
+    otherwise pair the current device's scratch array with memory the kernels cannot use)."""
+    q, w, c, r = _product(cuda_device, 8, 64, 16, seed=17)
+    m, k = q.shape
+    n = w.shape[0]
+    out = torch.zeros((1,), dtype=torch.int32, device=cuda_device)
+    host_c = c.cpu()
+    lib = nat.lib()
+    stream = ctypes.c_void_p(nat.stream_of(cuda_device))
+    status = lib.ima_freivalds_fp8_noalloc(q.data_ptr(), k, w.data_ptr(), k, host_c.data_ptr(), n, r.data_ptr(), m,
+                                           n, k, out.data_ptr(), stream)
+    assert status == nat.IMA_ERR_INVALID_ARGUMENT
+    host_out = torch.zeros((1,), dtype=torch.int32)
+    status = lib.ima_freivalds_fp8_noalloc(q.data_ptr(), k, w.data_ptr(), k, c.data_ptr(), n, r.data_ptr(), m, n, k,
+                                           host_out.data_ptr(), stream)
+    assert status == nat.IMA_ERR_INVALID_ARGUMENT
+    torch.cuda.synchronize(cuda_device)
+    assert int(out.item()) == 0 and int(host_out.item()) == 0
+    # the same call with device operands still works afterwards
+    assert _noalloc(q, w, c, r) == 0
+
+
 def test_noalloc_freivalds_rejects_sizes_beyond_its_scratch(cuda_device):
     lib = nat.lib()
     max_k = 65536
