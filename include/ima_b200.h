@@ -178,6 +178,14 @@ int ima_int_gemm_grouped(const ima_gemm_problem* problems, int count, int scheme
  * the GEMM (a persistent CTA never yields its SM, so a collective kernel queued behind a
  * full-machine GEMM launch would otherwise wait for it).  No reference counterpart. */
 int ima_set_gemm_sm_limit(int sms);
+/* Test knob of the failure-detection path (no reference counterpart): while stall_ns > 0,
+ * every later GEMM launch makes its MMA thread first wait, for stall_ns nanoseconds (at most
+ * 2 s), on an mbarrier that nothing arrives on.  The wait runs out: the kernel records
+ * IMA_ERR_TIMEOUT (where 3, detail -2) in the device status word, every role of each CTA
+ * stops, the loads and tensor-core work already in flight complete before the CTA frees
+ * its tensor memory, and the launch returns without writing outputs.  0 (the default)
+ * switches it off.  Process-wide, like ima_set_gemm_sm_limit. */
+int ima_set_gemm_wait_test(int64_t stall_ns);
 
 /* ---- A4: direct Hawkeye replay ---------------------------------------------
  * ref: hawkeye.py:222-275 hawkeye_fp8_sum (kernel hawkeye.py:127-219).
@@ -238,9 +246,12 @@ int ima_freivalds_fp8(const uint8_t* x_fp8, int64_t ldx, const uint8_t* w_fp8, i
  * argument, no allocation.  No counterpart in the reference.  The scratch vector lives in
  * a fixed device array of IMA_FREIVALDS_NOALLOC_MAX_K int64 (512 KiB) that every GPU
  * loading the library holds until exit; K above that maximum returns IMA_ERR_UNSUPPORTED.
- * The first call on a device looks the array's address up with that device current.  All
- * calls on a device share the array (each call clears it first), so calls whose work
- * overlaps on the GPU race; the caller still zeroes *mismatch_rows. */
+ * The first call on a device looks the array's address up with that device current.  The
+ * call uses the current device's array, so `stream` and every pointer argument must belong
+ * to the current device: a stream of another GPU, or a host or other-GPU pointer, returns
+ * IMA_ERR_INVALID_ARGUMENT before any launch.  All calls on a device share the array (each
+ * call clears it first), so calls whose work overlaps on the GPU race; the caller still
+ * zeroes *mismatch_rows. */
 #define IMA_FREIVALDS_NOALLOC_MAX_K 65536
 int ima_freivalds_fp8_noalloc(const uint8_t* x_fp8, int64_t ldx, const uint8_t* w_fp8, int64_t ldw,
                               const int64_t* c, int64_t ldc, const int64_t* r, int64_t M, int64_t N, int64_t K,

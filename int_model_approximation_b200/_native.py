@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ima_quantize_grouped": (_I32, [_VP, _I32, _VP]),
     "ima_int_gemm_grouped": (_I32, [_VP, _I32, _I32, _VP]),
     "ima_set_gemm_sm_limit": (_I32, [_I32]),
+    "ima_set_gemm_wait_test": (_I32, [_I64]),
     "ima_ipc_handle_bytes": (_I32, []),
     "ima_ipc_alloc": (_I32, [_I64, _VP, _VP]),
     "ima_ipc_free": (_I32, [_VP]),

@@ -96,7 +96,7 @@ struct GemmCfg {
     static constexpr int YST_OFFSET = CST_OFFSET + GM_EPI_WARPS * CST_BYTES;
     static constexpr int SCALE_OFFSET = YST_OFFSET + GM_EPI_WARPS * YST_BYTES;   // ws, bias: [warp][2][HALF]
     static constexpr int BAR_OFFSET = SCALE_OFFSET + 2 * GM_EPI_WARPS * 2 * HALF * 4;
-    static constexpr int TOTAL = BAR_OFFSET + (2 * STAGES + 2) * 8 + 16;
+    static constexpr int TOTAL = BAR_OFFSET + (2 * STAGES + 4) * 8 + 16;
     static constexpr int ALLOC = TOTAL + 1024;        // slack to align the base to 1024 B
 };
 
@@ -116,6 +116,7 @@ struct __align__(64) GemmBatch {
     GemmProblemDev p[GM_MAXP];
     int32_t tile_start[GM_MAXP + 1];
     int32_t n;
+    uint64_t stall_ns;              // test knob (ima_set_gemm_wait_test); 0 in normal use
 };
 
 IMA_DEVINL int find_problem(const GemmBatch& b, int64_t t) {
@@ -149,7 +150,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
     uint64_t* empty = full + L::STAGES;
     uint64_t* tmem_full = empty + L::STAGES;
     uint64_t* tmem_empty = tmem_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 1);
+    uint64_t* mma_drained = tmem_empty + 1;   // the MMA thread's final commit
+    uint64_t* never = mma_drained + 1;        // nothing arrives on it (the test stall waits here)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(never + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* s_ws = reinterpret_cast<float*>(smem + L::SCALE_OFFSET);   // [warp][2][HALF]
     float* s_bias = s_ws + GM_EPI_WARPS * 2 * HALF;                   // [warp][2][HALF]
@@ -164,6 +167,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
         }
         mbar_init(tmem_full, 1);
         mbar_init(tmem_empty, GM_EPI_WARPS * 32);
+        mbar_init(mma_drained, 1);
+        mbar_init(never, 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -178,6 +183,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
         uint32_t stage = 0, phase = 0;
+        uint64_t issued = 0;   // stages filled so far (drained below whatever happens)
         for (int64_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
             const int pi = find_problem(batch, t);
             const GemmProblemDev& P = batch.p[pi];
@@ -187,10 +193,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
             const CUtensorMap* ma = &batch.maps[pi][0];
             const CUtensorMap* mb = &batch.maps[pi][1];
             for (int kt = 0; kt < P.k_tiles; ++kt) {
-                if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, IMA_WHERE_GEMM_PRODUCER, (int)stage)) {
-                    *abort_flag = 1;
+                if (!mbar_wait_or_abort(&empty[stage], phase ^ 1u, abort_flag, IMA_WAIT_LIMIT_NS,
+                                        IMA_WHERE_GEMM_PRODUCER, (int)stage))
                     break;
-                }
+                ++issued;
                 unsigned char* sbase = smem + stage * L::STAGE_BYTES;
                 mbar_arrive_expect_tx(&full[stage], (uint32_t)L::STAGE_BYTES);
 #pragma unroll
@@ -201,20 +207,36 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                 if (++stage == (uint32_t)L::STAGES) { stage = 0; phase ^= 1u; }
             }
         }
+        // Drain: after an abort the MMA thread may not have consumed the last stages, so
+        // wait (bounded) until every TMA load issued into shared memory has landed before
+        // the CTA can exit.  Stage s received the fills of rounds 0 .. R_s - 1; the last one
+        // completes the phase of parity (R_s - 1) & 1 of full[s].
+        for (int s = 0; s < L::STAGES; ++s) {
+            const uint64_t rounds = issued / L::STAGES + ((uint64_t)s < issued % L::STAGES ? 1u : 0u);
+            if (rounds > 0)
+                mbar_wait_bounded(&full[s], (uint32_t)((rounds - 1) & 1u), IMA_WHERE_GEMM_PRODUCER, 100 + s);
+        }
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer ----------------
         constexpr uint32_t idesc = idesc_i8(GM_BM, NP * BN);
         uint32_t stage = 0, phase = 0, tphase = 0;
+        if (batch.stall_ns) {
+            // test knob: a wait that nothing ends runs out, records IMA_ERR_TIMEOUT and
+            // sets the abort flag; every role then drains and the kernel returns
+            mbar_wait_or_abort(never, 0u, abort_flag, batch.stall_ns, IMA_WHERE_GEMM_MMA, -2);
+        }
         for (int64_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
             const GemmProblemDev& P = batch.p[find_problem(batch, t)];
             // wait until the epilogue drained the previous tile and zeroed accumulators
             // NP .. NACC-1 (for the first tile: zeroed them at kernel start)
-            if (!mbar_wait_bounded(tmem_empty, tphase, IMA_WHERE_GEMM_MMA, -1)) { *abort_flag = 1; break; }
+            if (!mbar_wait_or_abort(tmem_empty, tphase, abort_flag, IMA_WAIT_LIMIT_NS, IMA_WHERE_GEMM_MMA, -1)) break;
             tphase ^= 1u;
             tc_fence_after();
+            bool fed = true;
             for (int kt = 0; kt < P.k_tiles; ++kt) {
-                if (!mbar_wait_bounded(&full[stage], phase, IMA_WHERE_GEMM_MMA, (int)stage)) {
-                    *abort_flag = 1;
+                if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, IMA_WAIT_LIMIT_NS, IMA_WHERE_GEMM_MMA,
+                                        (int)stage)) {
+                    fed = false;
                     break;
                 }
                 tc_fence_after();
@@ -233,8 +255,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                 mma_commit(&empty[stage]);
                 if (++stage == (uint32_t)L::STAGES) { stage = 0; phase ^= 1u; }
             }
+            if (!fed) break;
             mma_commit(tmem_full);
         }
+        // Drain: every MMA this thread issued completes before the CTA frees tensor memory
+        // (a commit with nothing outstanding arrives at once).
+        mma_commit(mma_drained);
+        mbar_wait_bounded(mma_drained, 0u, IMA_WHERE_GEMM_MMA, -3);
     } else if (warp >= 2) {
         // ---------------- epilogue ----------------
         const int ew = warp - 2;               // epilogue warp index 0..7
@@ -269,7 +296,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                 bias_t[i] = (P.bias && n < P.N) ? P.bias[n] : 0.0f;
             }
             __syncwarp();
-            bool ok = mbar_wait_bounded(tmem_full, tphase, IMA_WHERE_GEMM_EPILOGUE, -1);
+            bool ok = mbar_wait_or_abort(tmem_full, tphase, abort_flag, IMA_WAIT_LIMIT_NS, IMA_WHERE_GEMM_EPILOGUE, -1);
             __syncwarp();   // tcgen05.ld below is warp-collective
             if (!__all_sync(0xFFFFFFFFu, ok)) { *abort_flag = 1; break; }
             tphase ^= 1u;
@@ -473,6 +500,8 @@ int num_sms() {
 
 // Upper bound on the persistent GEMM grid (0: every SM); see ima_set_gemm_sm_limit.
 int g_gemm_sm_limit = 0;
+// Test knob of ima_set_gemm_wait_test: length of the stall wait (0: off).
+uint64_t g_gemm_stall_ns = 0;
 
 int gemm_grid_limit() {
     const int n = num_sms();
@@ -561,6 +590,7 @@ int run_grouped(const ima_gemm_problem* problems, int count, cudaStream_t stream
             b.n = k + 1;
         }
         b.tile_start[b.n] = tiles;
+        b.stall_ns = g_gemm_stall_ns;
         int rc = launch_batch<SCHEME>(b, stream);
         if (rc != IMA_OK) return rc;
     }
@@ -568,6 +598,12 @@ int run_grouped(const ima_gemm_problem* problems, int count, cudaStream_t stream
 }
 
 }  // namespace
+
+extern "C" int ima_set_gemm_wait_test(int64_t stall_ns) {
+    if (stall_ns < 0 || stall_ns > (int64_t)IMA_WAIT_LIMIT_NS) return IMA_ERR_INVALID_ARGUMENT;
+    g_gemm_stall_ns = (uint64_t)stall_ns;
+    return IMA_OK;
+}
 
 extern "C" int ima_set_gemm_sm_limit(int sms) {
     if (sms < 0) return IMA_ERR_INVALID_ARGUMENT;

@@ -48,6 +48,27 @@ IMA_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int where, int
     return true;
 }
 
+// As mbar_wait_bounded, with a caller-chosen limit, and giving up (without recording an
+// error) as soon as *abort becomes nonzero: another role of the CTA has given up already.
+// A timeout records IMA_ERR_TIMEOUT and sets *abort.
+IMA_DEVINL bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns, int where,
+                                   int detail) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = ima_globaltimer();
+    uint32_t spins = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if ((++spins & 63u) == 0) {
+            if (*abort) return false;
+            if (ima_globaltimer() - t0 > limit_ns) {
+                ima_record_error(IMA_ERR_TIMEOUT, where, detail);
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
 // ---------------------------------------------------------------------------
 // TMA: 3-D tile load global -> shared, completion counted on an mbarrier.
 // ---------------------------------------------------------------------------
