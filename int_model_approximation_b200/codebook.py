@@ -65,7 +65,10 @@ def per_token_fp8(x: torch.Tensor, *, codebook: bool = False, planes: bool = Fal
     dev = rows.device
     q = torch.empty((m, k), dtype=torch.uint8, device=dev)
     scale = torch.empty((m, 1), dtype=torch.float32, device=dev)
-    cb = torch.empty((m, k), dtype=torch.int32, device=dev) if codebook else None
+    with torch.inference_mode(False):
+        # a normal tensor even inside inference mode: its version counter lets a cache of
+        # its digit planes notice in-place edits (inference tensors have no counter)
+        cb = torch.empty((m, k), dtype=torch.int32, device=dev) if codebook else None
     cs = torch.empty((m, 1), dtype=torch.float32, device=dev) if codebook else None
     dp = DigitPlanes.empty(m, k, nat.IMA_SCHEME_DIGITS3, dev) if planes else None
     with torch.cuda.device(dev):
@@ -98,7 +101,8 @@ def codebook_planes_from_fp8(w_fp8: torch.Tensor, *, with_codebook_t: bool = Fal
     w = w_fp8.contiguous().view(torch.uint8)
     rows, k = w.shape
     dp = DigitPlanes.empty(rows, k, nat.IMA_SCHEME_DIGITS3, w.device)
-    cbt = torch.empty((k, rows), dtype=torch.int32, device=w.device) if with_codebook_t else None
+    with torch.inference_mode(False):   # versioned even inside inference mode (see per_token_fp8)
+        cbt = torch.empty((k, rows), dtype=torch.int32, device=w.device) if with_codebook_t else None
     with torch.cuda.device(w.device):
         nat.call(
             "ima_planes_from_fp8", w.data_ptr(), rows, k, k, dp.planes.data_ptr(), dp.ld, nat.ptr(cbt),

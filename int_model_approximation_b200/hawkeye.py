@@ -52,9 +52,14 @@ class HawkeyeOperand:
             )
         self._source = fp8
         self._version = nat.tensor_version(fp8)
+        self._data_ptr = fp8.data_ptr()
 
     def matches(self, fp8: torch.Tensor) -> bool:
-        return fp8 is self._source and nat.tensor_version(fp8) == self._version
+        """True while `fp8` is the staged tensor and unchanged since staging.  Inference
+        tensors have no version counter, so an in-place edit cannot be seen: they never match
+        (and are re-staged on every use)."""
+        return (fp8 is self._source and self._version is not None and nat.tensor_version(fp8) == self._version
+                and fp8.data_ptr() == self._data_ptr)
 
 
 def _validate_params(products_per_group: int, internal_width: int, zero_exponent: int) -> None:

@@ -54,10 +54,15 @@ _version_of = nat.tensor_version
 
 def _attach_planes(t: torch.Tensor, planes: DigitPlanes) -> None:
     """Remember the digit planes of an int32 operand on the tensor object itself, so that
-    _int32_matmul can skip re-expanding it; the planes are used only while the tensor's
-    version counter is unchanged (inference tensors have none and are taken as is)."""
+    _int32_matmul can skip re-expanding it.  The planes are used only while the tensor's
+    version counter is unchanged, so an in-place edit invalidates them.  Inference tensors
+    have no version counter: nothing is cached for them (this package creates its own
+    int32 operands as normal tensors, even inside inference mode, so they stay cacheable)."""
+    version = _version_of(t)
+    if version is None:
+        return
     try:
-        setattr(t, _PLANES_ATTR, (planes, _version_of(t)))
+        setattr(t, _PLANES_ATTR, (planes, version, t.data_ptr()))
     except (AttributeError, RuntimeError):
         pass
 
@@ -66,8 +71,19 @@ def _attached_planes(t: torch.Tensor) -> DigitPlanes | None:
     entry = getattr(t, _PLANES_ATTR, None)
     if entry is None:
         return None
-    planes, version = entry
-    return planes if version == _version_of(t) else None
+    planes, version, data_ptr = entry
+    current = _version_of(t)
+    if current is None or current != version or t.data_ptr() != data_ptr:
+        return None
+    return planes
+
+
+def _owned_copy(weight: torch.Tensor) -> torch.Tensor:
+    """A module-owned contiguous copy of an FP8 weight, created as a normal (versioned)
+    tensor even inside inference mode, so that the staging cached on it is dropped after
+    an in-place edit."""
+    with torch.inference_mode(False):
+        return weight.detach().clone(memory_format=torch.contiguous_format)
 
 
 # ---------------------------------------------------------------------------
@@ -247,7 +263,7 @@ class HawkeyeLinear(nn.Module):
         if weight.dtype != torch.float8_e4m3fn:
             raise RuntimeError(f"HawkeyeLinear needs FP8 weights, got {weight.dtype}")
         _require_cuda_tensor(weight, "Hawkeye FP8 weight")
-        self.register_buffer("weight", weight.detach().contiguous(), persistent=False)
+        self.register_buffer("weight", _owned_copy(weight), persistent=False)
         self.register_buffer("weight_scale", weight_scale.detach().to(torch.float32), persistent=False)
         stage_weight(self.weight)
         if bias is None:
@@ -285,7 +301,7 @@ class HawkeyeClassCountsLinear(nn.Module):
         if weight.dtype != torch.float8_e4m3fn:
             raise RuntimeError(f"HawkeyeClassCountsLinear needs FP8 weights, got {weight.dtype}")
         _require_cuda_tensor(weight, "Hawkeye exact FP8 weight")
-        self.register_buffer("weight", weight.detach().contiguous(), persistent=False)
+        self.register_buffer("weight", _owned_copy(weight), persistent=False)
         self.register_buffer("weight_scale", weight_scale.detach().to(torch.float32), persistent=False)
         stage_weight(self.weight)
         if bias is None:

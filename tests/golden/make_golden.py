@@ -156,6 +156,43 @@ def gen_codebook(entry) -> dict:
     return out
 
 
+def gen_int32_linear(entry) -> dict:
+    """The reference's Int32Linear (__main__.py:390-418: per-row / per-token int32 quantisers
+    with qmax = floor(sqrt((2^62 - 1) / K)), _int32_raw_matmul / _int32_matmul through the
+    Triton kernels, fp32 bias, cast back to x.dtype) on full-range int32 operands."""
+    out = {}
+    cases = {
+        "k300_bf16": (2 * 3, 300, 40, torch.bfloat16, True, 41),
+        "k37_f32": (5, 37, 24, torch.float32, False, 42),
+        "k2_f16": (4, 2, 5, torch.float16, True, 43),
+        "k896_bf16": (3, 896, 17, torch.bfloat16, True, 44),
+    }
+    for name, (m, k, n, dtype, with_bias, seed) in cases.items():
+        g = torch.Generator().manual_seed(seed)
+        weight = (torch.randn(n, k, generator=g) * 0.05).to(torch.float32)
+        bias = (torch.randn(n, generator=g) * 0.1).to(torch.float32) if with_bias else None
+        x = synthetic.student_t_activations(m, k, seed=seed + 1, outlier_fraction=0.02, dtype=dtype)
+        if name == "k300_bf16":
+            x = x.reshape(2, 3, k)
+        layer = entry.Int32Linear(weight, bias)
+        x_i32, x_scale = entry._per_token_int32(x, layer.qmax)
+        c = entry._int32_raw_matmul(x_i32, layer.weight_t)
+        y = layer(x)
+        out[f"{name}/x_f32"] = x.to(torch.float32).numpy()
+        out[f"{name}/x_dtype"] = np.array(str(dtype).replace("torch.", ""))
+        out[f"{name}/weight"] = weight.numpy()
+        if bias is not None:
+            out[f"{name}/bias"] = bias.numpy()
+        out[f"{name}/qmax"] = np.array(layer.qmax)
+        out[f"{name}/weight_t"] = layer.weight_t.numpy()
+        out[f"{name}/weight_scale"] = layer.weight_scale.numpy()
+        out[f"{name}/x_i32"] = x_i32.numpy()
+        out[f"{name}/x_scale"] = x_scale.numpy()
+        out[f"{name}/c"] = c.numpy()
+        out[f"{name}/y_f32"] = y.to(torch.float32).numpy()
+    return out
+
+
 def _hawkeye_kernel_fp32(hk, x_fp8, x_scale, w_fp8, w_scale, block_m=4, block_n=32):
     import triton
 
@@ -365,12 +402,13 @@ def main() -> None:
     if not checkout or not os.path.isdir(checkout):
         raise SystemExit("usage: make_golden.py <reference checkout>")
     entry, hk, hf = _load_reference(checkout)
-    sections = set(sys.argv[2:]) or {"quantize", "e4m3_cast", "codebook", "freivalds", "hawkeye", "class_counts",
-                                     "gfloat"}
+    sections = set(sys.argv[2:]) or {"quantize", "e4m3_cast", "codebook", "int32_linear", "freivalds", "hawkeye",
+                                     "class_counts", "gfloat"}
     gens = {
         "quantize": lambda: gen_quantize(entry),
         "e4m3_cast": gen_e4m3_cast,
         "codebook": lambda: gen_codebook(entry),
+        "int32_linear": lambda: gen_int32_linear(entry),
         "freivalds": lambda: gen_freivalds(entry, checkout),
         "hawkeye": lambda: gen_hawkeye(hk, hf),
         "class_counts": lambda: gen_class_counts(hf),

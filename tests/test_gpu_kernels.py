@@ -323,6 +323,33 @@ def test_int32_linear_matches_reference_forward(cuda_device, dtype, k):
     _assert_status_clean(cuda_device)
 
 
+@pytest.mark.parametrize("case", sorted(golden_cases(load_golden("int32_linear")).keys()))
+def test_int32_linear_matches_reference_fixture(cuda_device, case):
+    """Int32Linear against the reference's own Int32Linear run (tests/golden/int32_linear.npz):
+    the quantised weight and activations, the exact int64 product through _int32_raw_matmul
+    and the module output, bit for bit."""
+    d = golden_cases(load_golden("int32_linear"))[case]
+    dtype = getattr(torch, str(d["x_dtype"]))
+    x = torch.from_numpy(d["x_f32"]).to(dtype).to(cuda_device)
+    weight = torch.from_numpy(d["weight"]).to(cuda_device)
+    bias = torch.from_numpy(d["bias"]).to(cuda_device) if "bias" in d else None
+    layer = students.Int32Linear(weight, bias)
+    assert layer.qmax == float(d["qmax"])
+    assert torch.equal(layer.weight_t.cpu(), torch.from_numpy(d["weight_t"]))
+    assert torch.equal(layer.weight_scale.cpu(), torch.from_numpy(d["weight_scale"]))
+    x_i32, x_scale = students._per_token_int32(x, layer.qmax)
+    assert torch.equal(x_i32.cpu(), torch.from_numpy(d["x_i32"]))
+    assert torch.equal(x_scale.cpu(), torch.from_numpy(d["x_scale"]))
+    with students._Int32KernelProbe() as probe:
+        c = students._int32_raw_matmul(x_i32, layer.weight_t)
+        y = layer(x)
+    assert probe.count == 2
+    assert torch.equal(c.cpu(), torch.from_numpy(d["c"]))
+    assert y.dtype == dtype
+    assert torch.equal(_bits_any(y.cpu()), _bits_any(torch.from_numpy(d["y_f32"]).to(dtype)))
+    _assert_status_clean(cuda_device)
+
+
 def _bits_any(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous().view(torch.int32 if t.dtype == torch.float32 else torch.int16)
 
@@ -563,6 +590,45 @@ def test_inference_mode_keeps_the_codebook_scheme(cuda_device):
         x_i32, _ = students._per_token_fp8_int32(x)
         a, b = students._operand_planes(x_i32, layer.weight_t)
     assert a.scheme == b.scheme == nat.IMA_SCHEME_DIGITS3
+
+
+def test_in_place_edits_under_inference_mode_give_the_edited_product(cuda_device):
+    """int32 operands edited in place under torch.inference_mode() (the reference's driver
+    runs the student there) give the product of the edited values: the cached digit planes
+    of the package's own operands are dropped by the edit, and an inference tensor (no
+    version counter) is never served from a cache."""
+    w, ws = synthetic.normal_fp8_weights(48, 96, seed=31)
+    x = synthetic.student_t_activations(5, 96, seed=32).to(cuda_device)
+    with torch.inference_mode():
+        layer = students.CodebookLinear(w.to(cuda_device), ws.to(cuda_device), None)
+        x_i32, _ = students._per_token_fp8_int32(x)
+        first = students._int32_raw_matmul(x_i32, layer.weight_t)
+        x_i32[1, 3] += 7
+        layer.weight_t[5, 2] -= 11
+        edited = students._int32_raw_matmul(x_i32, layer.weight_t)
+        inf = torch.randint(-50, 50, (5, 96), dtype=torch.int32, device=cuda_device)
+        assert inf.is_inference()
+        c_inf = students._int32_raw_matmul(inf, layer.weight_t)
+        inf.add_(1)
+        c_inf_edited = students._int32_raw_matmul(inf, layer.weight_t)
+        a_cpu, b_cpu, inf_cpu = x_i32.cpu(), layer.weight_t.cpu(), inf.cpu()
+    assert not torch.equal(first, edited)
+    assert torch.equal(edited.cpu(), oracle.int_gemm(a_cpu, b_cpu))
+    assert torch.equal(c_inf_edited.cpu(), oracle.int_gemm(inf_cpu, b_cpu))
+    assert torch.equal(c_inf.cpu(), oracle.int_gemm(inf_cpu - 1, b_cpu))
+
+    # a Hawkeye student's staged weight follows an in-place edit of its weight buffer
+    xb = synthetic.student_t_activations(7, 96, seed=33).to(cuda_device)
+    with torch.inference_mode():
+        hl = students.HawkeyeLinear(w.to(cuda_device), ws.to(cuda_device), None)
+        hl(xb)
+        hl.weight[3].copy_(hl.weight[4])
+        y = hl(xb)
+        xq, xs = students._per_token_fp8(xb)
+        w_now = hl.weight.cpu()
+    ref = oracle.hawkeye(xq.cpu(), xs.cpu(), w_now, ws).to(torch.bfloat16)
+    assert torch.equal(y.cpu().view(torch.int16), ref.view(torch.int16))
+    _assert_status_clean(cuda_device)
 
 
 @pytest.mark.parametrize("kernel", ["codebook", "hawkeye", "hawkeye-class-counts"])

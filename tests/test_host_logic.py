@@ -346,3 +346,27 @@ def test_int32_path_source_has_no_float_gemm_or_cpu_fallbacks():
     assert not any(isinstance(node, ast.BinOp) and isinstance(node.op, ast.MatMult)
                    for node in ast.walk(ast.parse(source)))   # no `a @ b` on the path
     assert "ima_int_gemm" in _named_source(codebook, "int_gemm")
+
+
+def test_plane_cache_keys_on_the_version_counter():
+    """Cached digit planes are used only while the tensor is unchanged: an in-place edit
+    (also under inference mode, on the normal tensors this package creates) drops them,
+    and nothing is cached on inference tensors, which have no version counter."""
+    from int_model_approximation_b200.codebook import DigitPlanes
+
+    planes = DigitPlanes(torch.zeros((3, 4, 16), dtype=torch.int8), 4, 8, 3)
+    t = torch.zeros((4, 8), dtype=torch.int32)
+    students._attach_planes(t, planes)
+    assert students._attached_planes(t) is planes
+    t[1, 2] += 1
+    assert students._attached_planes(t) is None
+    with torch.inference_mode():
+        with torch.inference_mode(False):
+            u = torch.zeros((4, 8), dtype=torch.int32)
+        students._attach_planes(u, planes)
+        assert students._attached_planes(u) is planes
+        u.add_(3)
+        assert students._attached_planes(u) is None
+        inf = torch.zeros((4, 8), dtype=torch.int32)
+        students._attach_planes(inf, planes)
+        assert students._attached_planes(inf) is None

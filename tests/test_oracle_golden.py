@@ -5,6 +5,8 @@ These pin the oracle before it is trusted as the checker of the CUDA kernels.
 
 from __future__ import annotations
 
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -194,3 +196,28 @@ def test_gfloat_conversion_matches_reference_sweep():
     y = oracle.gfloat_to_float32(torch.from_numpy(g["sign"].astype(np.int32)), torch.from_numpy(g["exponent"]),
                                  torch.from_numpy(g["significand"]))
     assert np.array_equal(y.numpy().view(np.int32), g["f32_bits"])
+
+
+def _int32_linear_case(d):
+    dtype = getattr(torch, str(d["x_dtype"]))
+    x = torch.from_numpy(d["x_f32"]).to(dtype)
+    weight = torch.from_numpy(d["weight"])
+    bias = torch.from_numpy(d["bias"]) if "bias" in d else None
+    return x, weight, bias
+
+
+@pytest.mark.parametrize("case", sorted(golden_cases(load_golden("int32_linear")).keys()))
+def test_int32_linear_oracle_matches_the_reference_run(case):
+    """oracle.int32_linear against the reference's own Int32Linear (its Triton kernels run
+    by the interpreter on full-range int32 operands): quantised operands, the int64 product
+    and the module output, bit for bit."""
+    d = golden_cases(load_golden("int32_linear"))[case]
+    x, weight, bias = _int32_linear_case(d)
+    out = oracle.int32_linear(x, weight, bias)
+    assert out.dtype == x.dtype
+    assert torch.equal(out.to(torch.float32), torch.from_numpy(d["y_f32"]))
+    k = weight.shape[1]
+    qmax = float(min((1 << 31) - 1, int(math.sqrt(((1 << 62) - 1) / k))))
+    assert qmax == float(d["qmax"])
+    c = oracle.int_gemm(torch.from_numpy(d["x_i32"]), torch.from_numpy(d["weight_t"]))
+    assert torch.equal(c, torch.from_numpy(d["c"]))
