@@ -133,16 +133,38 @@ def measured_peaks() -> dict:
         return {}
 
 
-def profile_traffic(name: str) -> float | None:
-    """dram bytes per launch recorded from an ncu capture in profiles/<name>.md."""
-    path = os.path.join(ROOT, "profiles", f"{name}.md")
+def ncu_figure(kernel: str) -> dict | None:
+    """One kernel's figures from an ncu capture, as recorded in profiles/ncu_figures.json
+    (DRAM bytes per launch, instructions per unit of work, the capture command), plus
+    "current": whether the kernel's source files still hash to what was captured (False
+    means the figure predates the code being measured)."""
+    import hashlib
+
     try:
-        for line in open(path):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].strip())
-    except OSError:
+        with open(os.path.join(ROOT, "profiles", "ncu_figures.json")) as f:
+            rec = dict(json.load(f)[kernel])
+    except (OSError, ValueError, KeyError):
         return None
-    return None
+    h = hashlib.sha256()
+    try:
+        for src in rec.get("sources", []):
+            with open(os.path.join(ROOT, src), "rb") as f:
+                h.update(f.read())
+    except OSError:
+        rec["current"] = False
+        return rec
+    rec["current"] = h.hexdigest()[:16] == rec.get("sources_sha256_16")
+    return rec
+
+
+def int8_tensor_peak() -> tuple[float | None, str]:
+    """Dense int8 tensor peak for the GEMM roofline: twice the measured dense bf16 GEMM rate
+    (the int8 tensor path issues twice the bf16 MACs per cycle; MEASURED_PEAKS.json has no
+    int8 figure of its own)."""
+    peaks = measured_peaks()
+    if peaks.get("bf16_tflops"):
+        return 2.0 * float(peaks["bf16_tflops"]), "2 x MEASURED_PEAKS.json bf16_tflops (dense, burst)"
+    return None, "MEASURED_PEAKS.json absent"
 
 
 def build_workload(config: int, tokens: int, device, rank: int):
@@ -231,6 +253,8 @@ def run_hawkeye(args, emit: bool = True) -> dict:
     products = sum(tokens * s.n * s.k for s in shapes)
     int_peak = measured_int32_issue_rate(device)
     replay_terms = products / (times["replay"] * 1e-3)
+    fig = ncu_figure("hawkeye_replay_kernel") or {}
+    inst = fig.get("thread_instructions_per_product")
     res = {
         "workload": f"c2: 168 linears of Qwen2.5-0.5B shape, {tokens} tokens, direct Hawkeye K=32 replay",
         "outputs_per_s": outputs / (times["step"] * 1e-3),
@@ -239,13 +263,19 @@ def run_hawkeye(args, emit: bool = True) -> dict:
         "products_per_s": products / (times["step"] * 1e-3),
         "roofline": {
             "kernel": "hawkeye_replay_kernel",
-            "bound": "integer/FMA instruction issue",
-            "achieved": round(10.0 * replay_terms / 1e9, 1),
+            "bound": "instruction issue (integer ALU and FMA pipes)",
+            "achieved": round(inst * replay_terms / 1e9, 1) if inst else None,
             "peak": round(int_peak, 1),
-            "unit": "G int ops/s (10 int ops per product, the reference's per-product op count)",
-            "frac": round(10.0 * replay_terms / 1e9 / int_peak, 4),
-            "peak_source": "ima_int32_issue_probe (XOR+ADD chains, all SMs) measured in this run",
+            "unit": "G thread-instructions/s issued",
+            "frac": round(inst * replay_terms / 1e9 / int_peak, 4) if inst else None,
+            "instructions_per_product": inst,
+            "instructions_source": f"ncu inst_executed x 32 / products of one launch ({fig.get('command')}); "
+                                   f"capture matches the current source: {fig.get('current')}",
+            "peak_source": "ima_int32_issue_probe (XOR+ADD chains on every SM: the full issue rate) measured in "
+                           "this run",
             "products_per_s_replay_phase": replay_terms,
+            "reference_op_count": "the reference kernel's 10 integer ops per product would be "
+                                  f"{round(10.0 * replay_terms / 1e9, 1)} G ops/s equivalent",
         },
         "launches_per_step": stack.launches_per_forward(),
     }
@@ -331,6 +361,7 @@ def hawkeye_cpu_baseline(shapes, stack, bufs, budget_s: float) -> dict:
 
     rows = 64
     done_products, done_outputs, t_used, linears = 0.0, 0.0, 0.0, 0
+    parity_ok = True
     while t_used < budget_s and linears < len(shapes):
         i = linears
         s = shapes[i]
@@ -339,8 +370,11 @@ def hawkeye_cpu_baseline(shapes, stack, bufs, budget_s: float) -> dict:
         xs = bufs["scale"][i][:rows].cpu()
         wq, wsc = w.cpu(), ws.cpu()
         t0 = time.perf_counter()
-        oracle.hawkeye(xq, xs, wq, wsc)
+        ref = oracle.hawkeye(xq, xs, wq, wsc)
         t_used += time.perf_counter() - t0
+        # the CPU rows double as the parity check of the GPU replay (same operands)
+        parity_ok = parity_ok and torch.equal(bufs["y"][i][:rows].cpu().view(torch.int16),
+                                              ref.to(torch.bfloat16).view(torch.int16))
         done_products += float(rows) * s.n * s.k
         done_outputs += float(rows) * s.n
         linears += 1
@@ -352,6 +386,8 @@ def hawkeye_cpu_baseline(shapes, stack, bufs, budget_s: float) -> dict:
         "cores": threads,
         "kind": "port",
         "sample": f"{rows} token rows of each of the first {linears} linears, {t_used:.1f} s",
+        "parity": {"rows_checked": rows * linears, "linears_checked": linears, "ok": parity_ok,
+                   "what": "GPU bf16 outputs of the timed steps vs the CPU replay, bit for bit"},
     }
 
 
@@ -553,10 +589,14 @@ def run_b200(args) -> None:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(t.item())
     del e2e_graphs
+    plugin = None
+    if world == 1:
+        plugin = plugin_e2e(weights, xs, min(args.steps, 10), device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample(shapes, weights, xs, budget_s=args.cpu_seconds)
+        cpu = cpu_baseline_sample(shapes, weights, xs, budget_s=args.cpu_seconds, gpu_c=bufs["c"],
+                                  gpu_y=bufs["y"])
 
     if rank == 0:
         peaks = measured_peaks()
@@ -564,7 +604,10 @@ def run_b200(args) -> None:
         value = total_ops / (ms * 1e-3) / 1e12
         # DIGITS3: nine int8 digit products (3 x 3 planes) per exact product
         gemm_tc_ops = 9.0 * flops / (gemm_ms_per_step * 1e-3) / 1e12
-        traffic = profile_traffic("int_gemm_c1")
+        fig = ncu_figure("int_gemm_kernel<DIGITS3>") or {}
+        peak, peak_source = int8_tensor_peak()
+        if peak is None:
+            peak, peak_source = int8_peak, "torch._int_mm 8192^3 measured in this run (MEASURED_PEAKS.json absent)"
         line = {
             "metric": METRIC,
             "value": round(value, 3),
@@ -595,12 +638,18 @@ def run_b200(args) -> None:
                 "kernel": "int_gemm_kernel<DIGITS3>",
                 "bound": "tensor",
                 "achieved": round(gemm_tc_ops, 2),
-                "peak": round(int8_peak, 1),
+                "peak": round(peak, 1),
                 "unit": "TOPS (int8 tensor ops, 9 digit products per exact product)",
-                "limb_adjusted_peak_exact_tops": round(int8_peak / 9.0, 1),
-                "frac": round(gemm_tc_ops / int8_peak, 4),
-                "peak_source": "torch._int_mm 8192^3 best-of-10 measured in this run (MEASURED_PEAKS.json has no int8 figure)",
-                "traffic": traffic,
+                "limb_adjusted_peak_exact_tops": round(peak / 9.0, 1),
+                "frac": round(gemm_tc_ops / peak, 4),
+                "peak_source": peak_source,
+                "library_int8_gemm_tops": round(int8_peak, 1),
+                "library_int8_gemm": "torch._int_mm 8192^3 best-of-10 measured in this run (context: a library "
+                                     "int8 GEMM on this device)",
+                "traffic": fig.get("dram_bytes_per_launch"),
+                "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one grouped launch "
+                                   f"({fig.get('command')}); capture matches the current source: "
+                                   f"{fig.get('current')}") if fig else None,
                 "gemm_ms_per_step": round(gemm_ms_per_step, 4),
                 "gemm_launches_per_step": gemm_launches,
                 "exact_tops_gemm_only": round(flops / (gemm_ms_per_step * 1e-3) / 1e12, 3),
@@ -640,6 +689,7 @@ def run_b200(args) -> None:
                 "pipelining": "inputs of step i+1 in and outputs of step i-1 out while step i computes "
                               "(copy-in, compute and copy-out streams; two device buffer sets)",
             },
+            "e2e_plugin": plugin,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "measured_peaks": {k: peaks.get(k) for k in ("hbm_gbs", "bf16_tflops")},
@@ -662,19 +712,66 @@ def run_b200(args) -> None:
         torch.distributed.destroy_process_group()
 
 
-def cpu_baseline_sample(shapes, weights, xs, budget_s: float = 15.0) -> dict:
+def plugin_e2e(weights, xs, steps: int, device) -> dict:
+    """End to end through the reference-facing plugin: one students.CodebookLinear per
+    linear (built once, as the replacement pass builds them), called once per linear per
+    step on activations copied in from pinned host memory, its bf16 output copied back to
+    pinned host memory.  This is the per-call path the reference's driver takes (one module
+    forward per linear, __main__.py:754-773), so each call's ctypes, allocation and launch
+    overhead is inside the timed region; CUDA events on the launching stream time the
+    device timeline, host gaps included."""
+    from int_model_approximation_b200 import students
+
+    layers = [students.CodebookLinear(w, ws, b) for w, ws, b in weights]
+    host_x = [x.cpu().pin_memory() for x in xs]
+    host_y = [torch.empty((x.shape[0], lay.out_features), dtype=torch.bfloat16).pin_memory()
+              for x, lay in zip(xs, layers)]
+    ops = sum(2.0 * x.shape[0] * lay.out_features * lay.in_features for x, lay in zip(xs, layers))
+    stream = torch.cuda.current_stream(device)
+
+    def one_step() -> None:
+        for lay, hx, hy in zip(layers, host_x, host_y):
+            xd = hx.to(device, non_blocking=True)
+            hy.copy_(lay(xd), non_blocking=True)
+
+    for _ in range(2):
+        one_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        one_step()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {
+        "value": round(ops / (ms * 1e-3) / 1e12, 3),
+        "unit": "TOPS",
+        "ms_per_step": round(ms, 3),
+        "steps": steps,
+        "h2d_bytes_per_step": sum(x.numel() * 2 for x in host_x),
+        "d2h_bytes_per_step": sum(y.numel() * 2 for y in host_y),
+        "api": "students.CodebookLinear.forward, once per linear (168 calls per step), host bf16 activations "
+               "in, host bf16 outputs out; no Freivalds check (the reference's plugin has none)",
+    }
+
+
+def cpu_baseline_sample(shapes, weights, xs, budget_s: float = 15.0, gpu_c=None, gpu_y=None) -> dict:
     """The reference's CPU path (oracle port: torch quantiser, torch int64 matmul,
     fp32 rescale) on a bounded sample of the same workload: whole linears, cycling
     through the model, until the time budget is used.  torch's int64 matmul is
     single-threaded, so each linear's token rows are split over all host threads; the
     weight codes are prepared once per linear outside the timed region, as the
-    reference's CodebookLinear.__init__ does."""
+    reference's CodebookLinear.__init__ does.  The CPU results double as the parity check
+    of the GPU step: gpu_c / gpu_y (the int64 products and bf16 outputs the timed steps
+    wrote for the same inputs) are compared with them bit for bit, outside the CPU timing."""
     import oracle
 
     threads = os.cpu_count() or 1
     prev_threads = torch.get_num_threads()
     torch.set_num_threads(1)   # one row part per host thread instead of intra-op threads
     done_ops, t_used, linears = 0.0, 0.0, 0
+    rows_checked, parity_ok = 0, True
     i = 0
     try:
         while t_used < budget_s and linears < len(shapes):
@@ -684,14 +781,19 @@ def cpu_baseline_sample(shapes, weights, xs, budget_s: float = 15.0) -> dict:
             codes = oracle.fp8_codebook(wc).to(torch.int64)
             x = xs[i].cpu()
             t0 = time.perf_counter()
-            oracle.torch_cpu_codebook_linear(x, wc, wsc, bc, threads=threads, w_codes=codes)
+            c_ref, out_ref = oracle.torch_cpu_codebook_linear(x, wc, wsc, bc, threads=threads, w_codes=codes)
             t_used += time.perf_counter() - t0
+            if gpu_c is not None and gpu_y is not None:
+                same = torch.equal(gpu_c[i].cpu(), c_ref) and torch.equal(
+                    gpu_y[i].cpu().view(torch.int16), out_ref.view(torch.int16))
+                parity_ok = parity_ok and same
+                rows_checked += int(x.shape[0])
             done_ops += 2.0 * x.shape[0] * s.n * s.k
             linears += 1
             i += 1
     finally:
         torch.set_num_threads(prev_threads)
-    return {
+    out = {
         "value": round(done_ops / t_used / 1e12, 6),
         "unit": "TOPS",
         "cores": threads,
@@ -699,6 +801,11 @@ def cpu_baseline_sample(shapes, weights, xs, budget_s: float = 15.0) -> dict:
         "sample": f"{linears} whole linears of the c1 workload ({TOKENS} tokens each, rows split over "
                   f"{threads} threads), {t_used:.1f} s",
     }
+    if gpu_c is not None:
+        out["parity"] = {"rows_checked": rows_checked, "linears_checked": linears, "ok": parity_ok,
+                         "what": "GPU int64 products and bf16 outputs of the timed steps vs the CPU results, "
+                                 "bit for bit"}
+    return out
 
 
 def run_reference(args) -> None:
