@@ -269,6 +269,35 @@ int ima_freivalds_i32(const int32_t* a, int64_t lda, const int32_t* b, int64_t l
 int ima_class_presence(const uint8_t* fp8, int64_t rows, int64_t K, int64_t ld, int64_t pack_width, uint32_t* masks,
                        void* stream);
 
+/* The class-count engine.  ref: hawkeye_freivalds.py:1017-1246 exact_hawkeye_fp8_sum with
+ * its count products (:147-213, :593-704) and replays (:329-412 K5, :464-545 K6, :707-790 K7).
+ * Per group of 32 k, the counts count[a, b, m, n] of every (activation class a, weight class b)
+ * pair are formed on the tensor cores (one-hot int8 operands, int32 tensor memory): for each
+ * token row the (at most 32) classes present in the group against those of each weight row,
+ * i.e. every row and column of the reference's count product that can be nonzero.  The
+ * Hawkeye accumulator is replayed from the counts in the same kernel (output bit-identical to
+ * ima_hawkeye_replay), and every count tile is checked with a Freivalds fingerprint before it
+ * is discarded.
+ * Operands are staged once each with ima_class_count_prepare into a buffer of
+ * ima_class_count_operand_bytes(rows, K) bytes (16-byte aligned).
+ * Outputs: out_bf16 and/or out_f32 [M,N] = (gfloat * x_scale[m]) * w_scale[n];
+ * *mismatch_rows (device int32, zeroed by the caller) += slot rows whose count tile failed
+ * the fingerprint (0 for a correct run).  `seed` draws the fingerprint weights.
+ * tiles_out (optional, ima_class_count_tile_entries(M, N, K) int32) receives every count tile
+ * as the tensor cores formed it: tile (strip, group pair gp, tile t, group h) at index
+ * ((strip * ceil(G/2) + gp) * 8 + t) * 2 + h of [128 rows][256 cols], strip = sm + sn *
+ * ceil(M/4) covering tokens 4 sm .. 4 sm + 3 and weight rows 64 sn + 8 t .. + 7; row = 32 *
+ * token + activation slot, col = 32 * weight row + weight slot, value = count times the sign
+ * of the weight class (slots: ima_class_count_prepare's class order).  tiles_in (optional,
+ * same layout) replays and checks the given counts instead of the tensor-memory ones. */
+int64_t ima_class_count_operand_bytes(int64_t rows, int64_t K);
+int ima_class_count_prepare(const uint8_t* fp8, int64_t rows, int64_t K, int64_t ld, void* operand, void* stream);
+int64_t ima_class_count_tile_entries(int64_t M, int64_t N, int64_t K);
+int ima_class_count_replay(const void* x_operand, const void* w_operand, const float* x_scale, const float* w_scale,
+                           int64_t M, int64_t N, int64_t K, uint64_t seed, uint16_t* out_bf16, int64_t ld_bf16,
+                           float* out_f32, int64_t ld_f32, int32_t* mismatch_rows, int32_t* tiles_out,
+                           const int32_t* tiles_in, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

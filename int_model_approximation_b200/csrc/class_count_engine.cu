@@ -1,0 +1,641 @@
+// Class-count engine: the Freivalds-checkable count products of the hawkeye-class-counts
+// student formed on tcgen05 tensor cores and replayed, in the same kernel, into the Hawkeye
+// accumulator.
+//
+// ref: hawkeye_freivalds.py:1017-1246 (exact_hawkeye_fp8_sum), :860-1014 (packed groups),
+// :147-213 and :593-704 (the count products), :329-412 (K5, count product and replay in one
+// kernel: the model of this engine), :464-545 / :707-790 (K6/K7, the replay from counts).
+// Per group of 32 k the reference forms
+//     count[a, b, m, n] = #{k in the group : class(x[m,k]) = a, class(w[n,k]) = b}
+// as integer products A_flat @ B_flat (A_flat[(a, m), k] = [class(x[m,k]) = a], B_flat the
+// class indicators of the weights, optionally packed in base-64 lanes) and replays
+//     T = aligned(acc) + sum_{a,b} count[a,b,m,n] * trunc0((s_a s_b << 7) >> (maxe - e_a - e_b + 14)),
+// then normalises T to the 14-bit accumulator, group after group.
+//
+// Which products are formed.  Row (a, m) of A_flat is zero unless class a occurs in token m's
+// group, and a group has 32 k, so a token row has at most 32 classes per group (likewise each
+// weight row).  The engine forms exactly the rows and columns that can be nonzero: token row m
+// contributes 32 "slot" rows (its classes in first-occurrence order, unused slots all-zero),
+// weight row n 32 slot columns.  One tcgen05.mma of M = 128 (4 tokens x 32 slots), N = 256 (8
+// weight rows x 32 slots), K = 32 (one group) puts the count of every (a, b) class pair of 32
+// outputs into tensor memory.  Every nonzero lane of every product the reference forms is
+// such a count; the entries left out are zero by construction.  The weight one-hot carries the
+// class's sign (+1 / -1, int8), so a TMEM entry is the count times the weight class's sign.
+//
+// Fused replay.  An epilogue thread owns one slot row (token m, class a) and walks the 32
+// slot columns of a weight row n: with fa = |s_a| 2^e_a, fb = |s_b| 2^e_b and S = maxe + 7,
+//     bits(fma_rz(fa, fb, M_S)) = bits(M_S) + floor(fa fb / 2^S),    M_S = 1.5 * 2^(23+S)
+// (the product stays in the binade whose ulp is 2^S), so the thread accumulates
+// part = sum_b c_ab * bits(fma_rz(fa, fb, M_S)) with one FFMA.RZ and one IMAD per count.  The
+// 32 slot rows of a token are the 32 lanes of one warp: one REDUX adds sgn_a * part over them,
+// and the bits(M_S) offsets come out as bits(M_S) * (npos - nneg), the signed number of
+// present products of the output, known from the operands' masks.  The accumulator update is
+// then the direct replay's (hawkeye.cu), bit for bit.
+//
+// Freivalds fingerprint of every count tile.  Before a tile's counts are discarded, each
+// thread forms sum_col c[row, col] r[col] over the columns it read and compares it with
+// (A (B^T r))[row] over the same columns, computed from the operands, r = (r1 + 2^16 r2) with r1, r2 seeded per tile in [1, 15]: a product the
+// tensor cores got wrong fails the check (any single wrong count always; several wrong counts
+// cancel in both 16-bit halves with probability about 1/225).  Failed rows are counted in a
+// device word the caller reads.
+//
+// Modes for tests and offload: `tiles_out` receives every count tile as the tensor cores
+// formed it; `tiles_in` makes the epilogue replay (and check) counts supplied by the caller
+// instead of the tensor-memory ones.
+//
+// CTA (one per SM, persistent over "strips" of 4 tokens x 64 weight rows, all groups):
+//   warp 0     TMEM allocation (512 columns: two 256-column count tiles) and MMA issue
+//   warps 1-3  operand builders: one-hot A (per group pair) and B (per tile) in shared memory
+//              with the 64-byte swizzle, the class tables, the fingerprint vectors and each
+//              output's present-exponent maximum and signed present count
+//   warps 4-11 epilogue: warp (q = warp % 4, half) reads TMEM lanes 32q.. (token q of the
+//              strip) and half of the 8 weight rows of a tile; lane j keeps the accumulator of
+//              one output per tile
+// Every mbarrier wait is bounded and abort-aware; the MMA thread drains its work before the
+// CTA frees tensor memory.
+#include "sm100_primitives.cuh"
+
+namespace {
+
+constexpr int CE_GROUP = 32;
+constexpr int CE_TM = 4;                       // token rows per MMA tile: 4 x 32 slot rows = M 128
+constexpr int CE_TN = 8;                       // weight rows per MMA tile: 8 x 32 slot rows = N 256
+constexpr int CE_MAX_TILES = 8;                // MMA tiles per strip
+constexpr int CE_STRIP_N = CE_TN * CE_MAX_TILES;
+constexpr int CE_PITCH = 64;                   // staged rows are padded to a multiple of this
+constexpr int CE_BUILD_WARPS = 3;
+constexpr int CE_EPI_WARPS = 8;
+constexpr int CE_BUILDERS = 32 * CE_BUILD_WARPS;
+constexpr int CE_THREADS = 32 * (1 + CE_BUILD_WARPS + CE_EPI_WARPS);
+constexpr uint32_t CE_TMEM_COLS = 512;
+constexpr int CE_ABSENT_EXP = -8192;
+constexpr uint32_t CE_NO_SLOT = 0xFFu;
+constexpr int CE_WHERE = 6;                    // where-tag of this kernel's bounded waits
+
+// shared-memory layout (offsets from a 1024-byte aligned base)
+constexpr int CE_A_BYTES = 128 * 64;                            // 128 slot rows x 2 groups x 32 k
+constexpr int CE_B_BYTES = 256 * 64;
+constexpr int CE_OFF_A = 0;                                     // [2] buffers
+constexpr int CE_OFF_B = CE_OFF_A + 2 * CE_A_BYTES;             // [2]
+constexpr int CE_OFF_FA = CE_OFF_B + 2 * CE_B_BYTES;            // f32 [2 buf][2 h][128]
+constexpr int CE_OFF_FB = CE_OFF_FA + 2 * 2 * 128 * 4;          // f32 [2][2][256]
+constexpr int CE_OFF_RR = CE_OFF_FB + 2 * 2 * 256 * 4;          // u32 [2][2][256]
+constexpr int CE_OFF_BR = CE_OFF_RR + 2 * 2 * 256 * 4;          // s8  [2][2 h][2 half][2 vec][32 k]
+constexpr int CE_OFF_PE = CE_OFF_BR + 2 * 2 * 2 * 2 * 32;       // i32 [2][2 h][32 outputs]
+constexpr int CE_OFF_PN = CE_OFF_PE + 2 * 2 * 32 * 4;           // i32 [2][2][32]
+constexpr int CE_OFF_BAR = CE_OFF_PN + 2 * 2 * 32 * 4;
+constexpr int CE_NBAR = 13;
+constexpr int CE_TOTAL = CE_OFF_BAR + CE_NBAR * 8 + 16;
+constexpr int CE_ALLOC = CE_TOTAL + 1024;
+
+// Staged operand (ima_class_count_prepare), per group g and row r, pitch P rows:
+//   SL [G][P][32] u8    slot of k's class among the row's classes in the group (0xFF: zero element)
+//   CT [G][P][32] u8    e4m3 code of slot s's class (0 for unused slots)
+//   EX [G][P][16] u32   int16 pairs: effective exponent of k = 2j, 2j+1 (-8192 for a zero element)
+//   PS [G][P]     uint4 {bit k: k has a class, bit k: its sign, bit s: slot s's class is negative,
+//                        number of slots used}
+struct CeOperand {
+    uint8_t* sl;
+    uint8_t* ct;
+    uint32_t* ex;
+    uint4* ps;
+    int64_t pitch, groups;
+};
+
+__host__ __device__ inline int64_t ce_pitch(int64_t rows) { return ((rows + CE_PITCH - 1) / CE_PITCH) * CE_PITCH; }
+__host__ __device__ inline int64_t ce_groups(int64_t K) { return (K + CE_GROUP - 1) / CE_GROUP; }
+
+__host__ __device__ inline CeOperand ce_operand(const void* base, int64_t rows, int64_t K) {
+    CeOperand op;
+    op.pitch = ce_pitch(rows);
+    op.groups = ce_groups(K);
+    const int64_t recs = op.pitch * op.groups;
+    uint8_t* p = const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(base));
+    op.sl = p;
+    op.ct = p + recs * 32;
+    op.ex = reinterpret_cast<uint32_t*>(p + recs * 64);
+    op.ps = reinterpret_cast<uint4*>(p + recs * 128);
+    return op;
+}
+
+// One warp per (row, group): lane = k.  Classes are identified by their e4m3 code (a code
+// with a nonzero significand determines its class (e - 1) * 31 + (s + 15) and back).
+__global__ void __launch_bounds__(256) ce_prepare_kernel(const uint8_t* __restrict__ src, int64_t rows, int64_t K,
+                                                         int64_t ld, CeOperand op) {
+    const unsigned FULL = 0xFFFFFFFFu;
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int64_t g = blockIdx.y;
+    if (r >= op.pitch) return;                        // whole warps only
+    const int64_t k = g * CE_GROUP + lane;
+    const uint32_t b = (r < rows && k < K) ? (uint32_t)src[r * ld + k] : 0u;
+    const uint32_t eb = (b >> 3) & 15u, mant = b & 7u;
+    const uint32_t sig = eb ? (mant | 8u) : mant;
+    const bool present = sig != 0;
+    const unsigned peers = __match_any_sync(FULL, present ? b : (0x100u + (unsigned)lane));
+    const int leader = __ffs(peers) - 1;
+    const bool is_leader = present && leader == lane;
+    const unsigned leaders = __ballot_sync(FULL, is_leader);
+    const unsigned nslots = __popc(leaders);
+    const unsigned own_slot = __popc(leaders & ((1u << lane) - 1u));   // meaningful on leaders
+    const unsigned slot = __shfl_sync(FULL, own_slot, leader);
+    const unsigned slot_sign = __reduce_or_sync(FULL, (is_leader && (b & 0x80u)) ? (1u << own_slot) : 0u);
+    const int64_t rec = g * op.pitch + r;
+    op.sl[rec * 32 + lane] = present ? (uint8_t)slot : (uint8_t)CE_NO_SLOT;
+    if (is_leader) op.ct[rec * 32 + own_slot] = (uint8_t)b;
+    if ((unsigned)lane >= nslots) op.ct[rec * 32 + lane] = 0;
+    const int e = present ? (eb ? (int)eb : 1) : CE_ABSENT_EXP;
+    const int e_next = __shfl_down_sync(FULL, e, 1);
+    if ((lane & 1) == 0) op.ex[rec * 16 + (lane >> 1)] = ((uint32_t)e & 0xFFFFu) | ((uint32_t)e_next << 16);
+    const unsigned pres = __ballot_sync(FULL, present);
+    const unsigned sgn = __ballot_sync(FULL, present && (b & 0x80u));
+    if (lane == 0) op.ps[rec] = make_uint4(pres, sgn, slot_sign, nslots);
+}
+
+// |s| 2^e of an e4m3 code as an exact fp32 value (0 for a zero code).
+IMA_DEVINL float ce_magnitude(uint32_t code) {
+    const uint32_t eb = (code >> 3) & 15u, mant = code & 7u;
+    const uint32_t sig = eb ? (mant | 8u) : mant;
+    return (float)(sig << (eb ? eb : 1u));
+}
+
+// Seeded fingerprint weights r1, r2 in [1, 15] of count column `col` of a tile, packed r1 + 2^16 r2.
+IMA_DEVINL uint32_t ce_fingerprint_weight(uint64_t seed, uint64_t tile, uint32_t col) {
+    uint32_t h = (uint32_t)seed ^ (uint32_t)(seed >> 32) ^ (uint32_t)(tile * 0x9E3779B97F4A7C15ull >> 32) ^
+                 (col * 0x85EBCA6Bu);
+    h ^= h >> 15;
+    h *= 0x2C1B3C6Du;
+    h ^= h >> 12;
+    h *= 0x297A2D39u;
+    h ^= h >> 15;
+    return (1u + (h & 0xFFFFu) % 15u) | ((1u + (h >> 16) % 15u) << 16);
+}
+
+// One 16-byte chunk (16 k) of a one-hot slot row: byte = `one` where slot byte == s, else 0.
+IMA_DEVINL uint4 ce_onehot_chunk(uint4 slots, uint32_t s, uint32_t one) {
+    const uint32_t pat = s * 0x01010101u;
+    uint32_t w[4] = {slots.x ^ pat, slots.y ^ pat, slots.z ^ pat, slots.w ^ pat};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        // exact per-byte zero test: 0x80 in the bytes that are zero, no carries between bytes
+        const uint32_t z = ~(((w[j] & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | w[j] | 0x7F7F7F7Fu);
+        w[j] = (z >> 7) * one;
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Byte offset of (row, 16-byte chunk c) in a K-major tile of 64-byte rows with the 64-byte
+// swizzle (the layout a TMA SWIZZLE_64B load writes and umma_desc_sw64_kmajor describes).
+IMA_DEVINL uint32_t ce_sw64(uint32_t row, uint32_t c) { return row * 64u + ((c ^ ((row >> 1) & 3u)) << 4); }
+
+struct CeParams {
+    CeOperand a, b;
+    const float* xs;
+    const float* ws;
+    int64_t M, N, groups, strips_m, strips_n;
+    __nv_bfloat16* out_bf16;
+    int64_t ld_bf16;
+    float* out_f32;
+    int64_t ld_f32;
+    int32_t* mismatch;
+    int32_t* tiles_out;
+    const int32_t* tiles_in;
+    uint64_t seed;
+};
+
+__global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const __grid_constant__ CeParams P) {
+    extern __shared__ unsigned char ce_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(ce_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CE_OFF_BAR);
+    uint64_t* a_full = bars;           // [2] builders -> MMA, epilogue
+    uint64_t* a_empty = bars + 2;      // [2] MMA commit + epilogue warps -> builders
+    uint64_t* b_full = bars + 4;       // [2]
+    uint64_t* b_empty = bars + 6;      // [2]
+    uint64_t* t_full = bars + 8;       // [2] MMA commit -> epilogue
+    uint64_t* t_empty = bars + 10;     // [2] epilogue warps -> MMA
+    uint64_t* drained = bars + 12;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + CE_NBAR);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t G = P.groups;
+    const int64_t GP = (G + 1) / 2;
+    const int64_t strips = P.strips_m * P.strips_n;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&a_full[i], CE_BUILDERS);
+            mbar_init(&a_empty[i], 1 + CE_EPI_WARPS);
+            mbar_init(&b_full[i], CE_BUILDERS);
+            mbar_init(&b_empty[i], 1 + CE_EPI_WARPS);
+            mbar_init(&t_full[i], 1);
+            mbar_init(&t_empty[i], CE_EPI_WARPS);
+        }
+        mbar_init(drained, 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, CE_TMEM_COLS);
+        tmem_relinquish();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint64_t LIMIT = IMA_WAIT_LIMIT_NS;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = idesc_i8(128, 256);
+            uint64_t a_cnt = 0, u_cnt = 0;
+            bool ok = true;
+            for (int64_t sid = blockIdx.x; sid < strips && ok; sid += gridDim.x) {
+                const int64_t n0 = (sid / P.strips_m) * CE_STRIP_N;
+                const int tiles = (int)min((int64_t)CE_MAX_TILES, (P.N - n0 + CE_TN - 1) / CE_TN);
+                for (int64_t gp = 0; gp < GP && ok; ++gp) {
+                    const uint32_t abuf = a_cnt & 1u, aph = (a_cnt >> 1) & 1u;
+                    ++a_cnt;
+                    ok = mbar_wait_or_abort(&a_full[abuf], aph, abort_flag, LIMIT, CE_WHERE, 1);
+                    for (int t = 0; t < tiles && ok; ++t) {
+                        // B buffers alternate between units; each TMEM tile h is used once per unit
+                        const uint32_t ubuf = u_cnt & 1u, uph = (u_cnt >> 1) & 1u, tph = u_cnt & 1u;
+                        ++u_cnt;
+                        ok = mbar_wait_or_abort(&b_full[ubuf], uph, abort_flag, LIMIT, CE_WHERE, 2);
+                        for (int h = 0; h < 2 && ok; ++h) {
+                            ok = mbar_wait_or_abort(&t_empty[h], tph ^ 1u, abort_flag, LIMIT, CE_WHERE, 3);
+                            if (!ok) break;
+                            tc_fence_after();
+                            const uint32_t sa = smem_u32(smem + CE_OFF_A + abuf * CE_A_BYTES) + h * 32;
+                            const uint32_t sb = smem_u32(smem + CE_OFF_B + ubuf * CE_B_BYTES) + h * 32;
+                            mma_i8(tmem_base + (uint32_t)(h * 256), umma_desc_sw64_kmajor(sa), umma_desc_sw64_kmajor(sb),
+                                   idesc, 0u);
+                            mma_commit(&t_full[h]);
+                        }
+                        if (ok) mma_commit(&b_empty[ubuf]);
+                    }
+                    if (ok) mma_commit(&a_empty[abuf]);
+                }
+            }
+            // every MMA issued completes before tensor memory is freed
+            mma_commit(drained);
+            mbar_wait_bounded(drained, 0u, CE_WHERE, 9);
+        }
+    } else if (warp <= CE_BUILD_WARPS) {
+        // ---------------- operand builders ----------------
+        const int tb = threadIdx.x - 32;
+        const CeOperand A = P.a, B = P.b;
+        float* FA = reinterpret_cast<float*>(smem + CE_OFF_FA);
+        float* FB = reinterpret_cast<float*>(smem + CE_OFF_FB);
+        uint32_t* RR = reinterpret_cast<uint32_t*>(smem + CE_OFF_RR);
+        int8_t* BR = reinterpret_cast<int8_t*>(smem + CE_OFF_BR);
+        int32_t* PE = reinterpret_cast<int32_t*>(smem + CE_OFF_PE);
+        int32_t* PN = reinterpret_cast<int32_t*>(smem + CE_OFF_PN);
+        uint64_t a_cnt = 0, u_cnt = 0;
+        bool ok = true;
+        for (int64_t sid = blockIdx.x; sid < strips && ok; sid += gridDim.x) {
+            const int64_t m0 = (sid % P.strips_m) * CE_TM;
+            const int64_t n0 = (sid / P.strips_m) * CE_STRIP_N;
+            const int tiles = (int)min((int64_t)CE_MAX_TILES, (P.N - n0 + CE_TN - 1) / CE_TN);
+            for (int64_t gp = 0; gp < GP && ok; ++gp) {
+                const uint32_t abuf = a_cnt & 1u, aph = (a_cnt >> 1) & 1u;
+                ++a_cnt;
+                ok = mbar_wait_or_abort(&a_empty[abuf], aph ^ 1u, abort_flag, LIMIT, CE_WHERE, 4);
+                if (!ok) break;
+                // A: token classes of both groups of the pair
+                unsigned char* As = smem + CE_OFF_A + abuf * CE_A_BYTES;
+                for (int i = tb; i < 2 * 128; i += CE_BUILDERS) {
+                    const int h = i >> 7, row = i & 127;
+                    const int64_t g = 2 * gp + h;
+                    const int64_t rec = g * A.pitch + m0 + (row >> 5);
+                    const uint32_t code = g < G ? A.ct[rec * 32 + (row & 31)] : 0u;
+                    const float mag = ce_magnitude(code);
+                    FA[(abuf * 2 + h) * 128 + row] = (code & 0x80u) ? -mag : mag;
+                }
+                for (int i = tb; i < 128 * 4; i += CE_BUILDERS) {
+                    const int pair = i >> 5, s = i & 31;      // pair = (token, chunk)
+                    const int ml = pair >> 2, c = pair & 3, h = c >> 1;
+                    const int64_t g = 2 * gp + h;
+                    uint4 sl = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+                    if (g < G) sl = *reinterpret_cast<const uint4*>(A.sl + (g * A.pitch + m0 + ml) * 32 + (c & 1) * 16);
+                    const uint32_t row = (uint32_t)(ml * 32 + s);
+                    *reinterpret_cast<uint4*>(As + ce_sw64(row, c)) = ce_onehot_chunk(sl, (uint32_t)s, 1u);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&a_full[abuf]);
+                for (int t = 0; t < tiles && ok; ++t) {
+                    const uint32_t ubuf = u_cnt & 1u, uph = (u_cnt >> 1) & 1u;
+                    const uint64_t unit = u_cnt;
+                    ++u_cnt;
+                    ok = mbar_wait_or_abort(&b_empty[ubuf], uph ^ 1u, abort_flag, LIMIT, CE_WHERE, 5);
+                    if (!ok) break;
+                    const int64_t nt = n0 + (int64_t)t * CE_TN;
+                    unsigned char* Bs = smem + CE_OFF_B + ubuf * CE_B_BYTES;
+                    // class magnitudes and fingerprint weights of the 256 slot columns, both groups
+                    for (int i = tb; i < 2 * 256; i += CE_BUILDERS) {
+                        const int h = i >> 8, col = i & 255;
+                        const int64_t g = 2 * gp + h;
+                        const uint32_t code = g < G ? B.ct[(g * B.pitch + nt + (col >> 5)) * 32 + (col & 31)] : 0u;
+                        FB[(ubuf * 2 + h) * 256 + col] = ce_magnitude(code);
+                        RR[(ubuf * 2 + h) * 256 + col] = ce_fingerprint_weight(P.seed, unit * 2 + h, (uint32_t)col);
+                    }
+                    // one-hot weight slot rows carrying the class sign
+                    for (int i = tb; i < 256 * 4; i += CE_BUILDERS) {
+                        const int pair = i >> 5, s = i & 31;  // pair = (weight row, chunk)
+                        const int nl = pair >> 2, c = pair & 3, h = c >> 1;
+                        const int64_t g = 2 * gp + h;
+                        uint4 sl = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+                        uint32_t one = 1u;
+                        if (g < G) {
+                            const int64_t rec = g * B.pitch + nt + nl;
+                            sl = *reinterpret_cast<const uint4*>(B.sl + rec * 32 + (c & 1) * 16);
+                            one = ((B.ps[rec].z >> s) & 1u) ? 0xFFu : 1u;
+                        }
+                        const uint32_t row = (uint32_t)(nl * 32 + s);
+                        *reinterpret_cast<uint4*>(Bs + ce_sw64(row, c)) = ce_onehot_chunk(sl, (uint32_t)s, one);
+                    }
+                    // each output's largest present exponent sum and signed present count
+                    for (int i = tb; i < 2 * 32; i += CE_BUILDERS) {
+                        const int h = i >> 5, o = i & 31, ml = o >> 3, nl = o & 7;
+                        const int64_t g = 2 * gp + h;
+                        int pe = -16384, pn = 0;
+                        if (g < G) {
+                            const int64_t ra = g * A.pitch + m0 + ml, rb = g * B.pitch + nt + nl;
+                            uint32_t e2 = 0xC000C000u;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) e2 = __viaddmax_s16x2(A.ex[ra * 16 + j], B.ex[rb * 16 + j], e2);
+                            pe = max((int)(int16_t)(e2 & 0xFFFFu), (int)(int16_t)(e2 >> 16));
+                            const uint4 pa = A.ps[ra], pb = B.ps[rb];
+                            const uint32_t both = pa.x & pb.x;
+                            pn = __popc(both) - 2 * __popc(both & (pa.y ^ pb.y));
+                        }
+                        PE[(ubuf * 2 + h) * 32 + o] = pe;
+                        PN[(ubuf * 2 + h) * 32 + o] = pn;
+                    }
+                    // B^T r per k: the weight side of the fingerprint, two int8 vectors for
+                    // each half of the tile's weight rows (an epilogue warp sees the columns of
+                    // one half); the weights are recomputed from their hash rather than read
+                    // back from RR, so the builders need no barrier among themselves
+                    for (int i = tb; i < 2 * 2 * 32; i += CE_BUILDERS) {
+                        const int h = i >> 6, half = (i >> 5) & 1, k = i & 31;
+                        const int64_t g = 2 * gp + h;
+                        int s1 = 0, s2 = 0;
+                        if (g < G) {
+                            for (int nl = half * 4; nl < half * 4 + 4; ++nl) {
+                                const int64_t rec = g * B.pitch + nt + nl;
+                                const uint32_t slot = B.sl[rec * 32 + k];
+                                if (slot == CE_NO_SLOT) continue;
+                                const uint32_t rr = ce_fingerprint_weight(P.seed, unit * 2 + h, (uint32_t)(nl * 32 + slot));
+                                const bool neg = (B.ps[rec].z >> slot) & 1u;
+                                s1 += neg ? -(int)(rr & 0xFFFFu) : (int)(rr & 0xFFFFu);
+                                s2 += neg ? -(int)(rr >> 16) : (int)(rr >> 16);
+                            }
+                        }
+                        BR[(((ubuf * 2 + h) * 2 + half) * 2 + 0) * 32 + k] = (int8_t)s1;
+                        BR[(((ubuf * 2 + h) * 2 + half) * 2 + 1) * 32 + k] = (int8_t)s2;
+                    }
+                    fence_proxy_async_smem();
+                    mbar_arrive(&b_full[ubuf]);
+                }
+            }
+        }
+        if (!ok) *abort_flag = 1;
+    } else {
+        // ---------------- epilogue: replay from the counts ----------------
+        const int q = warp & 3;                      // token of the strip = TMEM lane quadrant
+        const int hn = (warp - 1 - CE_BUILD_WARPS) >> 2;   // which 4 of a tile's 8 weight rows
+        const unsigned FULL = 0xFFFFFFFFu;
+        const float* FA = reinterpret_cast<const float*>(smem + CE_OFF_FA);
+        const float* FB = reinterpret_cast<const float*>(smem + CE_OFF_FB);
+        const uint32_t* RR = reinterpret_cast<const uint32_t*>(smem + CE_OFF_RR);
+        const int8_t* BR = reinterpret_cast<const int8_t*>(smem + CE_OFF_BR);
+        const int32_t* PE = reinterpret_cast<const int32_t*>(smem + CE_OFF_PE);
+        const int32_t* PN = reinterpret_cast<const int32_t*>(smem + CE_OFF_PN);
+        const int row = q * 32 + lane;               // this thread's slot row of the MMA tile
+        uint64_t a_cnt = 0, u_cnt = 0;
+        bool ok = true;
+        for (int64_t sid = blockIdx.x; sid < strips && ok; sid += gridDim.x) {
+            const int64_t m0 = (sid % P.strips_m) * CE_TM;
+            const int64_t n0 = (sid / P.strips_m) * CE_STRIP_N;
+            const int tiles = (int)min((int64_t)CE_MAX_TILES, (P.N - n0 + CE_TN - 1) / CE_TN);
+            float acc = 0.0f;                        // lane j: output (m0 + q, n0 + 8 (j >> 2) + 4 hn + (j & 3))
+            for (int64_t gp = 0; gp < GP && ok; ++gp) {
+                const uint32_t abuf = a_cnt & 1u, aph = (a_cnt >> 1) & 1u;
+                ++a_cnt;
+                ok = mbar_wait_or_abort(&a_full[abuf], aph, abort_flag, LIMIT, CE_WHERE, 6);
+                if (!__all_sync(FULL, ok)) { ok = false; break; }
+                for (int t = 0; t < tiles && ok; ++t) {
+                    const uint32_t ubuf = u_cnt & 1u, uph = (u_cnt >> 1) & 1u, tph = u_cnt & 1u;
+                    ++u_cnt;
+                    ok = mbar_wait_or_abort(&b_full[ubuf], uph, abort_flag, LIMIT, CE_WHERE, 7);
+                    if (!__all_sync(FULL, ok)) { ok = false; break; }
+                    for (int h = 0; h < 2; ++h) {
+                        const int64_t g = 2 * gp + h;
+                        ok = mbar_wait_or_abort(&t_full[h], tph, abort_flag, LIMIT, CE_WHERE, 8);
+                        __syncwarp();
+                        if (!__all_sync(FULL, ok)) { ok = false; break; }
+                        tc_fence_after();
+                        // M_S of this warp's four outputs of the tile (owner lanes 4t .. 4t + 3)
+                        const int own_i = lane & 3;
+                        const int own_o = q * 8 + 4 * hn + own_i;
+                        const int tb = (int)(ubuf * 2 + h);
+                        const int pe = PE[tb * 32 + own_o];
+                        const int acc_e14 = (int)((__float_as_uint(acc) << 1) >> 24) - 133;
+                        const uint32_t ms_own = (uint32_t)max(pe, acc_e14) * (1u << 23) + ((143u << 23) | 0x400000u);
+                        uint32_t ms[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) ms[i] = __shfl_sync(FULL, ms_own, t * 4 + i);
+                        const float fa = FA[(abuf * 2 + h) * 128 + row];
+                        const float fa_abs = fabsf(fa);
+                        uint32_t part[4], fp = 0;
+                        const int64_t tile_id = (((sid * GP + gp) * CE_MAX_TILES + t) * 2 + h);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int col0 = (4 * hn + i) * 32;
+                            uint32_t c[32];
+                            if (P.tiles_in) {
+                                const int4* src = reinterpret_cast<const int4*>(P.tiles_in + (tile_id * 128 + row) * 256 + col0);
+#pragma unroll
+                                for (int v = 0; v < 8; ++v) {
+                                    const int4 x = src[v];
+                                    c[4 * v] = (uint32_t)x.x; c[4 * v + 1] = (uint32_t)x.y;
+                                    c[4 * v + 2] = (uint32_t)x.z; c[4 * v + 3] = (uint32_t)x.w;
+                                }
+                            } else {
+                                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + col0);
+                                uint32_t (&lo)[16] = *reinterpret_cast<uint32_t(*)[16]>(&c[0]);
+                                uint32_t (&hi)[16] = *reinterpret_cast<uint32_t(*)[16]>(&c[16]);
+                                tmem_ld16(taddr, lo);
+                                tmem_ld16(taddr + 16, hi);
+                                tmem_wait_ld();
+                            }
+                            if (P.tiles_out) {
+                                int4* dst = reinterpret_cast<int4*>(P.tiles_out + (tile_id * 128 + row) * 256 + col0);
+#pragma unroll
+                                for (int v = 0; v < 8; ++v)
+                                    dst[v] = make_int4((int)c[4 * v], (int)c[4 * v + 1], (int)c[4 * v + 2], (int)c[4 * v + 3]);
+                            }
+                            const float msf = __uint_as_float(ms[i]);
+                            const float4* fb4 = reinterpret_cast<const float4*>(FB + tb * 256 + col0);
+                            const uint4* rr4 = reinterpret_cast<const uint4*>(RR + tb * 256 + col0);
+                            uint32_t acc_i = 0;
+#pragma unroll
+                            for (int v = 0; v < 8; ++v) {
+                                const float4 fb = fb4[v];
+                                const uint4 rr = rr4[v];
+                                acc_i += c[4 * v] * __float_as_uint(__fmaf_rz(fa_abs, fb.x, msf));
+                                acc_i += c[4 * v + 1] * __float_as_uint(__fmaf_rz(fa_abs, fb.y, msf));
+                                acc_i += c[4 * v + 2] * __float_as_uint(__fmaf_rz(fa_abs, fb.z, msf));
+                                acc_i += c[4 * v + 3] * __float_as_uint(__fmaf_rz(fa_abs, fb.w, msf));
+                                fp += c[4 * v] * rr.x + c[4 * v + 1] * rr.y + c[4 * v + 2] * rr.z + c[4 * v + 3] * rr.w;
+                            }
+                            part[i] = acc_i;
+                        }
+                        // the counts are in registers: hand the tensor-memory tile back
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&t_empty[h]);
+                        if (g >= G) continue;                 // padding group of an odd group count
+                        // fingerprint: this row of the tile against (A (B^T r))[row]
+                        {
+                            const unsigned char* As = smem + CE_OFF_A + abuf * CE_A_BYTES;
+                            const uint4 a0 = *reinterpret_cast<const uint4*>(As + ce_sw64((uint32_t)row, 2 * h));
+                            const uint4 a1 = *reinterpret_cast<const uint4*>(As + ce_sw64((uint32_t)row, 2 * h + 1));
+                            const uint4* br1 = reinterpret_cast<const uint4*>(BR + ((tb * 2 + hn) * 2 + 0) * 32);
+                            const uint4* br2 = reinterpret_cast<const uint4*>(BR + ((tb * 2 + hn) * 2 + 1) * 32);
+                            const uint4 x0 = br1[0], x1 = br1[1], y0 = br2[0], y1 = br2[1];
+                            int e1 = 0, e2 = 0;
+                            e1 = __dp4a((int)a0.x, (int)x0.x, e1); e1 = __dp4a((int)a0.y, (int)x0.y, e1);
+                            e1 = __dp4a((int)a0.z, (int)x0.z, e1); e1 = __dp4a((int)a0.w, (int)x0.w, e1);
+                            e1 = __dp4a((int)a1.x, (int)x1.x, e1); e1 = __dp4a((int)a1.y, (int)x1.y, e1);
+                            e1 = __dp4a((int)a1.z, (int)x1.z, e1); e1 = __dp4a((int)a1.w, (int)x1.w, e1);
+                            e2 = __dp4a((int)a0.x, (int)y0.x, e2); e2 = __dp4a((int)a0.y, (int)y0.y, e2);
+                            e2 = __dp4a((int)a0.z, (int)y0.z, e2); e2 = __dp4a((int)a0.w, (int)y0.w, e2);
+                            e2 = __dp4a((int)a1.x, (int)y1.x, e2); e2 = __dp4a((int)a1.y, (int)y1.y, e2);
+                            e2 = __dp4a((int)a1.z, (int)y1.z, e2); e2 = __dp4a((int)a1.w, (int)y1.w, e2);
+                            const uint32_t expect = (uint32_t)e1 + ((uint32_t)e2 << 16);
+                            if (fp != expect) atomicAdd(P.mismatch, 1);
+                        }
+                        // sum sgn_a * part over the 32 slot rows of the token: one REDUX per weight row
+                        const uint32_t neg = fa < 0.0f ? 0xFFFFFFFFu : 0u;
+                        uint32_t tot[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) tot[i] = __reduce_add_sync(FULL, (part[i] ^ neg) - neg);
+                        if ((lane >> 2) == t) {
+                            const uint32_t m = ms_own;
+                            const uint32_t total = own_i == 0 ? tot[0] : own_i == 1 ? tot[1] : own_i == 2 ? tot[2] : tot[3];
+                            const int pn = PN[tb * 32 + own_o];
+                            const uint32_t amask = (uint32_t)((int32_t)__float_as_uint(acc) >> 31);
+                            const uint32_t av = __float_as_uint(__fmaf_rz(fabsf(acc), 1.0f, __uint_as_float(m))) - m;
+                            const uint32_t T = ((av ^ amask) - amask) + total - m * (uint32_t)pn;
+                            int32_t f = (int32_t)(m - ((23u << 23) + 0x400000u));   // (S + 127) << 23
+                            f = max(f, 0);
+                            const float v = __fmul_rn((float)(int32_t)T, __int_as_float(f));
+                            acc = __uint_as_float(__float_as_uint(v) & 0xFFFFFC00u);
+                        }
+                    }
+                    if (!ok) break;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&b_empty[ubuf]);
+                }
+                if (!ok) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_empty[abuf]);
+            }
+            if (!ok) break;
+            // outputs of the strip: gfloat = acc * 2^-20, y = (gfloat * xs) * ws
+            const int64_t m = m0 + q;
+            const int64_t n = n0 + 8 * (lane >> 2) + 4 * hn + (lane & 3);
+            if ((lane >> 2) < tiles && m < P.M && n < P.N) {
+                const float gf = __fmul_rn(acc, 9.5367431640625e-07f);
+                const float y = __fmul_rn(__fmul_rn(gf, P.xs[m]), P.ws[n]);
+                if (P.out_bf16) P.out_bf16[m * P.ld_bf16 + n] = __float2bfloat16_rn(y);
+                if (P.out_f32) P.out_f32[m * P.ld_f32 + n] = y;
+            }
+        }
+        if (!ok) *abort_flag = 1;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, CE_TMEM_COLS);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t ima_class_count_operand_bytes(int64_t rows, int64_t K) {
+    if (rows < 0 || K < 0) return 0;
+    return ce_pitch(rows) * ce_groups(K) * 144;
+}
+
+int ima_class_count_prepare(const uint8_t* fp8, int64_t rows, int64_t K, int64_t ld, void* operand, void* stream) {
+    if (!fp8 || !operand || rows < 0 || K < 0 || ld < K) return IMA_ERR_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(operand) & 15) return IMA_ERR_INVALID_ARGUMENT;
+    const int64_t pitch = ce_pitch(rows), groups = ce_groups(K);
+    if (pitch == 0 || groups == 0) return IMA_OK;
+    if (groups > 65535) return IMA_ERR_UNSUPPORTED;
+    CeOperand op = ce_operand(operand, rows, K);
+    dim3 grid((unsigned)(pitch / 8), (unsigned)groups);
+    ce_prepare_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(fp8, rows, K, ld, op);
+    return IMA_LAUNCH_STATUS();
+}
+
+int64_t ima_class_count_tile_entries(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const int64_t strips = ((M + CE_TM - 1) / CE_TM) * ((N + CE_STRIP_N - 1) / CE_STRIP_N);
+    const int64_t gp = (ce_groups(K) + 1) / 2;
+    return strips * gp * CE_MAX_TILES * 2 * 128 * 256;
+}
+
+int ima_class_count_replay(const void* x_operand, const void* w_operand, const float* x_scale, const float* w_scale,
+                           int64_t M, int64_t N, int64_t K, uint64_t seed, uint16_t* out_bf16, int64_t ld_bf16,
+                           float* out_f32, int64_t ld_f32, int32_t* mismatch_rows, int32_t* tiles_out,
+                           const int32_t* tiles_in, void* stream) {
+    if (!x_operand || !w_operand || !x_scale || !w_scale || !mismatch_rows || M < 0 || N < 0 || K < 0)
+        return IMA_ERR_INVALID_ARGUMENT;
+    if (!out_bf16 && !out_f32) return IMA_ERR_INVALID_ARGUMENT;
+    if ((out_bf16 && ld_bf16 < N) || (out_f32 && ld_f32 < N)) return IMA_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(x_operand) & 15) || (reinterpret_cast<uintptr_t>(w_operand) & 15) ||
+        (reinterpret_cast<uintptr_t>(tiles_out) & 15) || (reinterpret_cast<uintptr_t>(tiles_in) & 15))
+        return IMA_ERR_INVALID_ARGUMENT;
+    if (M == 0 || N == 0) return IMA_OK;
+    CeParams p;
+    p.a = ce_operand(x_operand, M, K);
+    p.b = ce_operand(w_operand, N, K);
+    p.xs = x_scale;
+    p.ws = w_scale;
+    p.M = M;
+    p.N = N;
+    p.groups = ce_groups(K);
+    p.strips_m = (M + CE_TM - 1) / CE_TM;
+    p.strips_n = (N + CE_STRIP_N - 1) / CE_STRIP_N;
+    p.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+    p.ld_bf16 = ld_bf16;
+    p.out_f32 = out_f32;
+    p.ld_f32 = ld_f32;
+    p.mismatch = mismatch_rows;
+    p.tiles_out = tiles_out;
+    p.tiles_in = tiles_in;
+    p.seed = seed;
+    const int64_t strips = p.strips_m * p.strips_n;
+    int rc = ima_note_cuda(
+        cudaFuncSetAttribute(class_count_replay_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CE_ALLOC));
+    if (rc != IMA_OK) return rc;
+    if (K == 0) {
+        // no products: every output is the zero accumulator
+        if (out_bf16) rc = ima_note_cuda(cudaMemset2DAsync(out_bf16, ld_bf16 * 2, 0, N * 2, M, (cudaStream_t)stream));
+        if (rc == IMA_OK && out_f32)
+            rc = ima_note_cuda(cudaMemset2DAsync(out_f32, ld_f32 * 4, 0, N * 4, M, (cudaStream_t)stream));
+        return rc;
+    }
+    const int grid = (int)(strips < num_sms() ? strips : num_sms());
+    class_count_replay_kernel<<<grid, CE_THREADS, CE_ALLOC, (cudaStream_t)stream>>>(p);
+    return IMA_LAUNCH_STATUS();
+}
+
+}  // extern "C"

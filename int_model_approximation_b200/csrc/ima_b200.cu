@@ -6,3 +6,4 @@
 #include "freivalds.cu"
 #include "int_gemm.cu"
 #include "class_counts.cu"
+#include "class_count_engine.cu"

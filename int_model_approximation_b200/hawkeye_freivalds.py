@@ -5,25 +5,27 @@ same HawkeyeFreivaldsStats (:22-33), the same exact_hawkeye_fp8_sum signature an
 parameter validation (:1017-1050, :878-886), bit-identical bf16 output and
 identical stats.
 
-How the B200 path works.  The reference materialises one packed count product per
+How the B200 path works.  The reference forms one packed count product per
 (activation-class chunk, weight-class chunk) pair of every pack and replays the
-Hawkeye accumulator from those counts.  Summing count(a, b) * aligned(a, b, maxe)
-over class pairs is a regrouping of the per-k sum the direct replay computes, so the
-output is produced by the direct replay engine (csrc/hawkeye.cu) without
-materialising any counts.  The class bookkeeping that defines the checkable products
-(one class-presence kernel over all packs, one host read instead of one
-torch.unique sync per group) yields the same product count and class maxima as the
-reference; each checkable product bumps the active int32 probe once, exactly as the
-reference's raw_matmul calls do.
+Hawkeye accumulator from those counts.  Here the class-count engine
+(csrc/class_count_engine.cu) forms the counts on the tcgen05 tensor cores -- for each
+group of 32 k, the counts of every (activation class, weight class) pair of every
+output, i.e. every row and column of the reference's product that can be nonzero --
+checks each count tile with a Freivalds fingerprint, and replays the accumulator from
+the counts in the same kernel; the counts never reach HBM.  The class bookkeeping that
+defines the reference's checkable products (one class-presence kernel over all packs,
+one host read instead of one torch.unique sync per group) yields the same product count
+and class maxima as the reference.
 
-A caller that injects its own raw_matmul (and does not ask for fused_replay) gets the
-reference's materialised products: the same one-hot / lane-packed operands in the same
-order, one call per checkable product.  Each returned product is Freivalds-checked on the
-GPU against its operands (a wrong product raises), and the output, a function of the
-counts, is then produced by the direct replay, bit-identical to replaying the counts.
-The count-product helpers keep the reference's names and layouts
-(hawkeye_freivalds.py:39-57, :147-213, :593-704, :840-841), so code written against them
-runs unchanged.
+raw_matmul.  With raw_matmul None (what HawkeyeClassCountsLinear passes) the engine
+forms the products and the active int32 probe is bumped once per product the reference
+would have sent through its _int32_raw_matmul.  Any callable instead receives the
+reference's products themselves -- the same one-hot / lane-packed operands in the same
+order, one call per checkable product (as the reference calls it; _int32_raw_matmul
+bumps the probe per call) -- and every product it returns is Freivalds-checked on the
+GPU (a wrong one raises); the output is the engine's.  The count-product helpers keep
+the reference's names and layouts (hawkeye_freivalds.py:39-57, :147-213, :593-704,
+:840-841), so code written against them runs unchanged.
 """
 
 from __future__ import annotations
@@ -34,7 +36,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _native as nat
-from .hawkeye import HawkeyeOperand, _validate_params, hawkeye_replay, stage_weight
+from .hawkeye import _validate_params
 
 FP32_SIGNIFICAND_WIDTH = 24
 FP32_MIN_NONZERO_EXPONENT = -126
@@ -288,6 +290,112 @@ def class_count_stats(
     )
 
 
+class ClassCountOperand:
+    """An e4m3 matrix [rows, K] staged for the class-count engine: per row and group of 32 k,
+    the slot of each element's class among the row's classes in the group, the classes'
+    codes, exponent pairs and present/sign masks (ima_class_count_prepare)."""
+
+    def __init__(self, fp8: torch.Tensor):
+        if fp8.device.type != "cuda":
+            raise RuntimeError("Hawkeye class-count replay is CUDA-only")
+        raw = fp8.contiguous().view(torch.uint8)
+        self.rows, self.k = int(raw.shape[0]), int(raw.shape[1])
+        self.device = raw.device
+        nbytes = int(nat.lib().ima_class_count_operand_bytes(self.rows, self.k))
+        self.buffer = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=raw.device)
+        with torch.cuda.device(raw.device):
+            nat.call("ima_class_count_prepare", raw.data_ptr(), self.rows, self.k, self.k, self.buffer.data_ptr(),
+                     nat.stream_of(raw.device))
+        self._source = fp8
+        self._version = nat.tensor_version(fp8)
+        self._data_ptr = fp8.data_ptr()
+
+    def matches(self, fp8: torch.Tensor) -> bool:
+        """True while `fp8` is the staged tensor and unchanged since staging (never for
+        inference tensors, whose in-place edits leave no trace)."""
+        return (fp8 is self._source and self._version is not None and nat.tensor_version(fp8) == self._version
+                and fp8.data_ptr() == self._data_ptr)
+
+    def tables(self) -> dict[str, torch.Tensor]:
+        """The staged tables as tensors (views of the buffer): slots [G, P, 32] uint8, codes
+        [G, P, 32] uint8 (rows padded to the pitch P)."""
+        pitch = -(-max(self.rows, 1) // 64) * 64
+        groups = -(-self.k // 32)
+        recs = pitch * groups
+        return {"slots": self.buffer[: recs * 32].view(groups, pitch, 32),
+                "codes": self.buffer[recs * 32: recs * 64].view(groups, pitch, 32)}
+
+
+def stage_class_count_weight(w_fp8: torch.Tensor) -> ClassCountOperand:
+    """Stage a weight for the class-count engine once and cache the staging on the tensor."""
+    cached = getattr(w_fp8, "_ima_class_count_operand", None)
+    if cached is not None and cached.matches(w_fp8):
+        return cached
+    op = ClassCountOperand(w_fp8)
+    try:
+        w_fp8._ima_class_count_operand = op
+    except (AttributeError, RuntimeError):
+        pass
+    return op
+
+
+_SEED_COUNTER = [0x5EED]
+
+
+def class_count_replay(
+    x_op: ClassCountOperand,
+    w_op: ClassCountOperand,
+    x_scale: torch.Tensor,
+    w_scale: torch.Tensor,
+    *,
+    seed: int | None = None,
+    out: torch.Tensor | None = None,
+    out_f32: torch.Tensor | None = None,
+    mismatch: torch.Tensor | None = None,
+    tiles_out: torch.Tensor | None = None,
+    tiles_in: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """The engine on staged operands: returns (bf16 [M, N] or the given outputs, the device
+    int32 count of slot rows whose count tile failed the fingerprint).  No host sync.
+    tiles_out / tiles_in: int32 [ima_class_count_tile_entries(M, N, K)] count tiles as the
+    tensor cores formed them / counts to replay instead (layout in include/ima_b200.h)."""
+    m, n, k = x_op.rows, w_op.rows, x_op.k
+    if w_op.k != k:
+        raise RuntimeError(f"Hawkeye shape mismatch: K={k} vs K={w_op.k}")
+    dev = x_op.device
+    xs = x_scale.reshape(-1).to(torch.float32).contiguous()
+    ws = w_scale.reshape(-1).to(torch.float32).contiguous()
+    if xs.numel() != m or ws.numel() != n:
+        raise RuntimeError(f"Hawkeye scales have {xs.numel()} and {ws.numel()} entries, expected {m} and {n}")
+    if out is None and out_f32 is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    if mismatch is None:
+        mismatch = torch.zeros((1,), dtype=torch.int32, device=dev)
+    entries = int(nat.lib().ima_class_count_tile_entries(m, n, k))
+    for label, t in (("tiles_out", tiles_out), ("tiles_in", tiles_in)):
+        if t is not None and (t.dtype != torch.int32 or t.numel() < entries or not t.is_contiguous()):
+            raise RuntimeError(f"{label} must be a contiguous int32 tensor of at least {entries} entries")
+    nat.require_device(dev, ("weight operand", w_op.buffer), ("x_scale", xs), ("w_scale", ws), ("output", out),
+                       ("fp32 output", out_f32), ("mismatch counter", mismatch), ("tiles_out", tiles_out),
+                       ("tiles_in", tiles_in))
+    if seed is None:
+        _SEED_COUNTER[0] += 1
+        seed = _SEED_COUNTER[0] * 0x9E3779B97F4A7C15 % (1 << 64)
+    with torch.cuda.device(dev):
+        nat.call(
+            "ima_class_count_replay", x_op.buffer.data_ptr(), w_op.buffer.data_ptr(), xs.data_ptr(), ws.data_ptr(),
+            m, n, k, int(seed) % (1 << 64), nat.ptr(out), out.stride(0) if out is not None else n, nat.ptr(out_f32),
+            out_f32.stride(0) if out_f32 is not None else n, mismatch.data_ptr(), nat.ptr(tiles_out),
+            nat.ptr(tiles_in), nat.stream_of(dev),
+        )
+    return (out if out is not None else out_f32), mismatch
+
+
+def count_tile_entries(m: int, n: int, k: int) -> int:
+    """int32 entries of the engine's count-tile layout for an [m, k] x [n, k] product."""
+    return int(nat.lib().ima_class_count_tile_entries(m, n, k))
+
+
 class _CheckedMatmul:
     """Wraps an injected raw_matmul: every product it returns is Freivalds-checked on the GPU
     against its operands before use, and calls are counted."""
@@ -405,13 +513,12 @@ def exact_hawkeye_fp8_sum(
 ) -> tuple[torch.Tensor, HawkeyeFreivaldsStats]:
     """Replay Hawkeye exactly from Freivalds-checkable class-count products.
 
-    ref: hawkeye_freivalds.py:1017-1246.  With raw_matmul None or this package's own
-    _int32_raw_matmul (what HawkeyeClassCountsLinear passes, as the reference does) the
-    counts are folded into the replay engine and never materialised; the active int32 probe
-    is bumped once per product the reference would have sent through _int32_raw_matmul.
-    Any other raw_matmul receives the reference's products, one call each, and every result
-    is Freivalds-checked (RuntimeError if one fails).  The output is the direct replay in
-    both cases.
+    ref: hawkeye_freivalds.py:1017-1246.  The class-count engine forms the count products
+    on the tensor cores, fingerprints every count tile and replays the accumulator from the
+    counts (RuntimeError if a tile fails its check).  With raw_matmul None the active int32
+    probe is bumped once per product the reference would have sent through
+    _int32_raw_matmul; a callable receives the reference's products, one call each (each
+    result Freivalds-checked, RuntimeError if one fails).
     """
     if count_dtype not in {torch.int8, torch.int32}:
         raise ValueError(f"count_dtype must be torch.int8 or torch.int32, got {count_dtype}")
@@ -468,9 +575,9 @@ def exact_hawkeye_fp8_sum(
         packed_group_lanes=packed_group_lanes,
     )
     reference_calls = 0 if (fused_replay and packed_count_lanes == 1) else stats.total_checkable_products
-    from . import students
-
-    if raw_matmul is None or raw_matmul is students._int32_raw_matmul:
+    if raw_matmul is None:
+        # the engine forms these products; the probe counts them as the reference's
+        # _int32_raw_matmul launches would have been counted
         _bump_probe(reference_calls)
     else:
         made = _materialise_count_products(
@@ -481,7 +588,10 @@ def exact_hawkeye_fp8_sum(
         if made != reference_calls:
             raise RuntimeError(f"internal: {made} count products formed, {reference_calls} expected")
 
-    x_op = HawkeyeOperand(x_fp8)
-    w_op = stage_weight(w_fp8)
-    out = hawkeye_replay(x_op, w_op, xs.contiguous(), w_scale)
+    x_op = ClassCountOperand(x_fp8)
+    w_op = stage_class_count_weight(w_fp8)
+    out, bad = class_count_replay(x_op, w_op, xs.contiguous(), w_scale)
+    failed = int(bad.item())   # one host read per call, like the reference's class-list syncs
+    if failed:
+        raise RuntimeError(f"class-count products failed the Freivalds fingerprint on {failed} rows")
     return out, stats

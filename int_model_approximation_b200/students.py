@@ -22,7 +22,7 @@ import torch.nn as nn
 from . import _native as nat
 from .codebook import DigitPlanes, codebook_planes_from_fp8, int_gemm, per_token_fp8, planes_from_int32
 from .hawkeye import hawkeye_fp8_sum, stage_weight
-from .hawkeye_freivalds import exact_hawkeye_fp8_sum
+from .hawkeye_freivalds import exact_hawkeye_fp8_sum, stage_class_count_weight
 
 STUDENT_KERNEL = os.environ.get("IMA_STUDENT_KERNEL", "codebook")
 SUPPORTED_STUDENT_KERNELS = {"codebook", "hawkeye", "hawkeye-class-counts"}
@@ -303,7 +303,7 @@ class HawkeyeClassCountsLinear(nn.Module):
         _require_cuda_tensor(weight, "Hawkeye exact FP8 weight")
         self.register_buffer("weight", _owned_copy(weight), persistent=False)
         self.register_buffer("weight_scale", weight_scale.detach().to(torch.float32), persistent=False)
-        stage_weight(self.weight)
+        stage_class_count_weight(self.weight)
         if bias is None:
             self.bias = None
         else:
@@ -315,12 +315,14 @@ class HawkeyeClassCountsLinear(nn.Module):
         _require_cuda_tensor(x, "Hawkeye exact input")
         in_shape = x.shape
         x_fp8, x_scale = _per_token_fp8(x)
+        # raw_matmul None: the class-count engine forms the checkable count products on the
+        # tensor cores (the reference passes its _int32_raw_matmul here, which forms them)
         y, _stats = exact_hawkeye_fp8_sum(
             x_fp8,
             x_scale,
             self.weight,
             self.weight_scale,
-            _int32_raw_matmul,
+            None,
             products_per_group=HAWKEYE_PRODUCTS_PER_GROUP,
             internal_width=HAWKEYE_INTERNAL_WIDTH,
             zero_exponent=HAWKEYE_ZERO_EXPONENT,
