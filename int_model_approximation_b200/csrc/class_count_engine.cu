@@ -83,8 +83,19 @@ constexpr int CE_OFF_RR = CE_OFF_FB + 2 * 2 * 256 * 4;          // u32 [2][2][25
 constexpr int CE_OFF_BR = CE_OFF_RR + 2 * 2 * 256 * 4;          // s8  [2][2 h][2 half][2 vec][32 k]
 constexpr int CE_OFF_PE = CE_OFF_BR + 2 * 2 * 2 * 2 * 32;       // i32 [2][2 h][32 outputs]
 constexpr int CE_OFF_PN = CE_OFF_PE + 2 * 2 * 32 * 4;           // i32 [2][2][32]
-constexpr int CE_OFF_BAR = CE_OFF_PN + 2 * 2 * 32 * 4;
-constexpr int CE_NBAR = 13;
+// staging of one unit's operand records (the 8 weight rows and the 4 tokens, both groups)
+constexpr int CE_ST_SLB = 0;                                    // u8  [2 h][8][32]
+constexpr int CE_ST_CTB = CE_ST_SLB + 2 * CE_TN * 32;           // u8  [2][8][32]
+constexpr int CE_ST_EXB = CE_ST_CTB + 2 * CE_TN * 32;           // u32 [2][8][16]
+constexpr int CE_ST_PSB = CE_ST_EXB + 2 * CE_TN * 64;           // uint4 [2][8]
+constexpr int CE_ST_SLA = CE_ST_PSB + 2 * CE_TN * 16;           // u8  [2][4][32]
+constexpr int CE_ST_CTA = CE_ST_SLA + 2 * CE_TM * 32;
+constexpr int CE_ST_EXA = CE_ST_CTA + 2 * CE_TM * 32;           // u32 [2][4][16]
+constexpr int CE_ST_PSA = CE_ST_EXA + 2 * CE_TM * 64;           // uint4 [2][4]
+constexpr int CE_STAGE_BYTES = CE_ST_PSA + 2 * CE_TM * 16;      // 3456
+constexpr int CE_OFF_STAGE = CE_OFF_PN + 2 * 2 * 32 * 4;        // [2] staging buffers
+constexpr int CE_OFF_BAR = CE_OFF_STAGE + 2 * CE_STAGE_BYTES;
+constexpr int CE_NBAR = 17;
 constexpr int CE_TOTAL = CE_OFF_BAR + CE_NBAR * 8 + 16;
 constexpr int CE_ALLOC = CE_TOTAL + 1024;
 
@@ -203,10 +214,106 @@ struct CeParams {
     uint64_t seed;
 };
 
+// As mbar_wait_or_abort, but each try_wait may suspend the thread (up to 20 us, or until the
+// phase completes) instead of spinning, so waiting warps leave their issue slots to the warps
+// that work.
+IMA_DEVINL bool ce_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+        : "memory");
+    return ok != 0;
+}
+
+IMA_DEVINL bool ce_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns, int detail) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = ima_globaltimer();
+    while (!ce_try_wait_sleep(bar, parity)) {
+        if (*abort) return false;
+        if (ima_globaltimer() - t0 > limit_ns) {
+            ima_record_error(IMA_ERR_TIMEOUT, CE_WHERE, detail);
+            *abort = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+// Position of a CTA's work: strip `sid` (stride gridDim.x), group pair `gp`, tile `t` of the strip.
+struct CeCursor {
+    int64_t sid, gp;
+    int t, tiles;
+    bool valid;
+};
+
+IMA_DEVINL int ce_strip_tiles(const CeParams& P, int64_t sid) {
+    const int64_t n0 = (sid / P.strips_m) * CE_STRIP_N;
+    return (int)min((int64_t)CE_MAX_TILES, (P.N - n0 + CE_TN - 1) / CE_TN);
+}
+
+IMA_DEVINL CeCursor ce_cursor_first(const CeParams& P, int64_t strips) {
+    CeCursor c;
+    c.sid = blockIdx.x;
+    c.gp = 0;
+    c.t = 0;
+    c.valid = c.sid < strips;
+    c.tiles = c.valid ? ce_strip_tiles(P, c.sid) : 0;
+    return c;
+}
+
+IMA_DEVINL void ce_cursor_next(CeCursor& c, const CeParams& P, int64_t strips, int64_t GP) {
+    if (++c.t < c.tiles) return;
+    c.t = 0;
+    if (++c.gp < GP) return;
+    c.gp = 0;
+    c.sid += gridDim.x;
+    c.valid = c.sid < strips;
+    c.tiles = c.valid ? ce_strip_tiles(P, c.sid) : 0;
+}
+
+// 1-D bulk copy global -> shared, completion counted on an mbarrier (no multicast).
+IMA_DEVINL void ce_bulk_copy(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Stage the operand records of the unit at `c` into one staging buffer: for both groups of the
+// pair, the 8 weight rows' and the 4 tokens' slots, codes, exponent pairs and masks (16 copies
+// of 64 to 512 bytes, all 16-byte aligned).
+IMA_DEVINL void ce_stage_unit(const CeParams& P, const CeCursor& c, unsigned char* dst, uint64_t* bar) {
+    const int64_t m0 = (c.sid % P.strips_m) * CE_TM;
+    const int64_t nt = (c.sid / P.strips_m) * CE_STRIP_N + (int64_t)c.t * CE_TN;
+    const int live = (2 * c.gp + 1 < P.groups) ? 2 : 1;
+    mbar_arrive_expect_tx(bar, (uint32_t)(live * (CE_TN + CE_TM) * (32 + 32 + 64 + 16)));
+    for (int h = 0; h < live; ++h) {
+        const int64_t g = 2 * c.gp + h;
+        const int64_t rb = g * P.b.pitch + nt, ra = g * P.a.pitch + m0;
+        ce_bulk_copy(dst + CE_ST_SLB + h * CE_TN * 32, P.b.sl + rb * 32, CE_TN * 32, bar);
+        ce_bulk_copy(dst + CE_ST_CTB + h * CE_TN * 32, P.b.ct + rb * 32, CE_TN * 32, bar);
+        ce_bulk_copy(dst + CE_ST_EXB + h * CE_TN * 64, P.b.ex + rb * 16, CE_TN * 64, bar);
+        ce_bulk_copy(dst + CE_ST_PSB + h * CE_TN * 16, P.b.ps + rb, CE_TN * 16, bar);
+        ce_bulk_copy(dst + CE_ST_SLA + h * CE_TM * 32, P.a.sl + ra * 32, CE_TM * 32, bar);
+        ce_bulk_copy(dst + CE_ST_CTA + h * CE_TM * 32, P.a.ct + ra * 32, CE_TM * 32, bar);
+        ce_bulk_copy(dst + CE_ST_EXA + h * CE_TM * 64, P.a.ex + ra * 16, CE_TM * 64, bar);
+        ce_bulk_copy(dst + CE_ST_PSA + h * CE_TM * 16, P.a.ps + ra, CE_TM * 16, bar);
+    }
+}
+
+// MODE: CE_TENSOR_COUNTS (normal), CE_DUMP_TILES (also write every count tile to tiles_out),
+// CE_SUPPLIED_TILES (replay and check the counts in tiles_in instead of the tensor-memory ones).
+enum { CE_TENSOR_COUNTS = 0, CE_DUMP_TILES = 1, CE_SUPPLIED_TILES = 2 };
+
+template <int MODE>
 __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const __grid_constant__ CeParams P) {
-    extern __shared__ unsigned char ce_raw[];
-    unsigned char* smem =
-        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(ce_raw) + 1023) & ~(uintptr_t)1023);
+    extern __shared__ __align__(1024) unsigned char ce_raw[];
+    // align to 1024 bytes by pointer arithmetic on the shared array itself, so that every
+    // access below stays a shared-memory access (not a generic one)
+    unsigned char* smem = ce_raw + ((1024u - (smem_u32(ce_raw) & 1023u)) & 1023u);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CE_OFF_BAR);
     uint64_t* a_full = bars;           // [2] builders -> MMA, epilogue
     uint64_t* a_empty = bars + 2;      // [2] MMA commit + epilogue warps -> builders
@@ -214,7 +321,7 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
     uint64_t* b_empty = bars + 6;      // [2]
     uint64_t* t_full = bars + 8;       // [2] MMA commit -> epilogue
     uint64_t* t_empty = bars + 10;     // [2] epilogue warps -> MMA
-    uint64_t* drained = bars + 12;
+    uint64_t* drained = bars + 12;       // bars 13-16: the builders' staging barriers
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + CE_NBAR);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -233,6 +340,10 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
             mbar_init(&t_empty[i], CE_EPI_WARPS);
         }
         mbar_init(drained, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars[13 + i], 1);              // staging copies: one expect_tx arrival
+            mbar_init(&bars[15 + i], CE_BUILDERS);
+        }
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -257,14 +368,14 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                 for (int64_t gp = 0; gp < GP && ok; ++gp) {
                     const uint32_t abuf = a_cnt & 1u, aph = (a_cnt >> 1) & 1u;
                     ++a_cnt;
-                    ok = mbar_wait_or_abort(&a_full[abuf], aph, abort_flag, LIMIT, CE_WHERE, 1);
+                    ok = ce_wait(&a_full[abuf], aph, abort_flag, LIMIT, 1);
                     for (int t = 0; t < tiles && ok; ++t) {
                         // B buffers alternate between units; each TMEM tile h is used once per unit
                         const uint32_t ubuf = u_cnt & 1u, uph = (u_cnt >> 1) & 1u, tph = u_cnt & 1u;
                         ++u_cnt;
-                        ok = mbar_wait_or_abort(&b_full[ubuf], uph, abort_flag, LIMIT, CE_WHERE, 2);
+                        ok = ce_wait(&b_full[ubuf], uph, abort_flag, LIMIT, 2);
                         for (int h = 0; h < 2 && ok; ++h) {
-                            ok = mbar_wait_or_abort(&t_empty[h], tph ^ 1u, abort_flag, LIMIT, CE_WHERE, 3);
+                            ok = ce_wait(&t_empty[h], tph ^ 1u, abort_flag, LIMIT, 3);
                             if (!ok) break;
                             tc_fence_after();
                             const uint32_t sa = smem_u32(smem + CE_OFF_A + abuf * CE_A_BYTES) + h * 32;
@@ -284,119 +395,149 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
         }
     } else if (warp <= CE_BUILD_WARPS) {
         // ---------------- operand builders ----------------
+        // Builder thread 0 also stages each unit's operand records (the 8 weight rows and the 4
+        // tokens of both groups: slots, codes, exponent pairs, masks) into shared memory with
+        // bulk asynchronous copies, one unit ahead; the builders then work from shared memory.
         const int tb = threadIdx.x - 32;
-        const CeOperand A = P.a, B = P.b;
+        const bool loader = tb == 0;
         float* FA = reinterpret_cast<float*>(smem + CE_OFF_FA);
         float* FB = reinterpret_cast<float*>(smem + CE_OFF_FB);
         uint32_t* RR = reinterpret_cast<uint32_t*>(smem + CE_OFF_RR);
         int8_t* BR = reinterpret_cast<int8_t*>(smem + CE_OFF_BR);
         int32_t* PE = reinterpret_cast<int32_t*>(smem + CE_OFF_PE);
         int32_t* PN = reinterpret_cast<int32_t*>(smem + CE_OFF_PN);
-        uint64_t a_cnt = 0, u_cnt = 0;
+        uint64_t* s_full = bars + 13;    // [2] staging copies landed (expect_tx)
+        uint64_t* s_empty = bars + 15;   // [2] builders done with a staging buffer
+        CeCursor cur = ce_cursor_first(P, strips), nxt = cur;
+        uint64_t u = 0, a_cnt = 0, issued = 0;
         bool ok = true;
-        for (int64_t sid = blockIdx.x; sid < strips && ok; sid += gridDim.x) {
-            const int64_t m0 = (sid % P.strips_m) * CE_TM;
-            const int64_t n0 = (sid / P.strips_m) * CE_STRIP_N;
-            const int tiles = (int)min((int64_t)CE_MAX_TILES, (P.N - n0 + CE_TN - 1) / CE_TN);
-            for (int64_t gp = 0; gp < GP && ok; ++gp) {
-                const uint32_t abuf = a_cnt & 1u, aph = (a_cnt >> 1) & 1u;
+        if (loader && nxt.valid) {
+            ce_stage_unit(P, nxt, smem + CE_OFF_STAGE, &s_full[0]);
+            ++issued;
+            ce_cursor_next(nxt, P, strips, GP);
+        }
+        while (cur.valid && ok) {
+            const uint32_t sbuf = (uint32_t)(u & 1u), sph = (uint32_t)((u >> 1) & 1u);
+            if (loader && nxt.valid) {
+                // unit u + 1 goes into the other buffer, last read by unit u - 1
+                const uint64_t v = u + 1;
+                ok = ce_wait(&s_empty[v & 1u], (uint32_t)(((v >> 1) & 1u) ^ 1u), abort_flag, LIMIT, 10);
+                if (ok) {
+                    ce_stage_unit(P, nxt, smem + CE_OFF_STAGE + (v & 1u) * CE_STAGE_BYTES, &s_full[v & 1u]);
+                    ++issued;
+                    ce_cursor_next(nxt, P, strips, GP);
+                }
+            }
+            ok = ok && ce_wait(&s_full[sbuf], sph, abort_flag, LIMIT, 11);
+            if (!ok) break;
+            const unsigned char* S = smem + CE_OFF_STAGE + sbuf * CE_STAGE_BYTES;
+            const uint8_t* SLB = S + CE_ST_SLB;
+            const uint8_t* CTB = S + CE_ST_CTB;
+            const uint32_t* EXB = reinterpret_cast<const uint32_t*>(S + CE_ST_EXB);
+            const uint4* PSB = reinterpret_cast<const uint4*>(S + CE_ST_PSB);
+            const uint8_t* SLA = S + CE_ST_SLA;
+            const uint8_t* CTA = S + CE_ST_CTA;
+            const uint32_t* EXA = reinterpret_cast<const uint32_t*>(S + CE_ST_EXA);
+            const uint4* PSA = reinterpret_cast<const uint4*>(S + CE_ST_PSA);
+            const int64_t gp = cur.gp;
+            if (cur.t == 0) {
+                // A of the group pair: token classes of both groups
+                const uint32_t abuf = (uint32_t)(a_cnt & 1u), aph = (uint32_t)((a_cnt >> 1) & 1u);
                 ++a_cnt;
-                ok = mbar_wait_or_abort(&a_empty[abuf], aph ^ 1u, abort_flag, LIMIT, CE_WHERE, 4);
+                ok = ce_wait(&a_empty[abuf], aph ^ 1u, abort_flag, LIMIT, 4);
                 if (!ok) break;
-                // A: token classes of both groups of the pair
                 unsigned char* As = smem + CE_OFF_A + abuf * CE_A_BYTES;
                 for (int i = tb; i < 2 * 128; i += CE_BUILDERS) {
                     const int h = i >> 7, row = i & 127;
-                    const int64_t g = 2 * gp + h;
-                    const int64_t rec = g * A.pitch + m0 + (row >> 5);
-                    const uint32_t code = g < G ? A.ct[rec * 32 + (row & 31)] : 0u;
+                    const uint32_t code = 2 * gp + h < G ? CTA[(h * CE_TM + (row >> 5)) * 32 + (row & 31)] : 0u;
                     const float mag = ce_magnitude(code);
                     FA[(abuf * 2 + h) * 128 + row] = (code & 0x80u) ? -mag : mag;
                 }
                 for (int i = tb; i < 128 * 4; i += CE_BUILDERS) {
-                    const int pair = i >> 5, s = i & 31;      // pair = (token, chunk)
-                    const int ml = pair >> 2, c = pair & 3, h = c >> 1;
-                    const int64_t g = 2 * gp + h;
+                    const uint32_t row = (uint32_t)(i >> 2), c = (uint32_t)(i & 3);   // 8 rows x 4 chunks per warp store
+                    const uint32_t h = c >> 1;
                     uint4 sl = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-                    if (g < G) sl = *reinterpret_cast<const uint4*>(A.sl + (g * A.pitch + m0 + ml) * 32 + (c & 1) * 16);
-                    const uint32_t row = (uint32_t)(ml * 32 + s);
-                    *reinterpret_cast<uint4*>(As + ce_sw64(row, c)) = ce_onehot_chunk(sl, (uint32_t)s, 1u);
+                    if (2 * gp + h < G)
+                        sl = *reinterpret_cast<const uint4*>(SLA + (h * CE_TM + (row >> 5)) * 32 + (c & 1u) * 16);
+                    *reinterpret_cast<uint4*>(As + ce_sw64(row, c)) = ce_onehot_chunk(sl, row & 31u, 1u);
                 }
                 fence_proxy_async_smem();
                 mbar_arrive(&a_full[abuf]);
-                for (int t = 0; t < tiles && ok; ++t) {
-                    const uint32_t ubuf = u_cnt & 1u, uph = (u_cnt >> 1) & 1u;
-                    const uint64_t unit = u_cnt;
-                    ++u_cnt;
-                    ok = mbar_wait_or_abort(&b_empty[ubuf], uph ^ 1u, abort_flag, LIMIT, CE_WHERE, 5);
-                    if (!ok) break;
-                    const int64_t nt = n0 + (int64_t)t * CE_TN;
-                    unsigned char* Bs = smem + CE_OFF_B + ubuf * CE_B_BYTES;
-                    // class magnitudes and fingerprint weights of the 256 slot columns, both groups
-                    for (int i = tb; i < 2 * 256; i += CE_BUILDERS) {
-                        const int h = i >> 8, col = i & 255;
-                        const int64_t g = 2 * gp + h;
-                        const uint32_t code = g < G ? B.ct[(g * B.pitch + nt + (col >> 5)) * 32 + (col & 31)] : 0u;
-                        FB[(ubuf * 2 + h) * 256 + col] = ce_magnitude(code);
-                        RR[(ubuf * 2 + h) * 256 + col] = ce_fingerprint_weight(P.seed, unit * 2 + h, (uint32_t)col);
-                    }
-                    // one-hot weight slot rows carrying the class sign
-                    for (int i = tb; i < 256 * 4; i += CE_BUILDERS) {
-                        const int pair = i >> 5, s = i & 31;  // pair = (weight row, chunk)
-                        const int nl = pair >> 2, c = pair & 3, h = c >> 1;
-                        const int64_t g = 2 * gp + h;
-                        uint4 sl = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-                        uint32_t one = 1u;
-                        if (g < G) {
-                            const int64_t rec = g * B.pitch + nt + nl;
-                            sl = *reinterpret_cast<const uint4*>(B.sl + rec * 32 + (c & 1) * 16);
-                            one = ((B.ps[rec].z >> s) & 1u) ? 0xFFu : 1u;
-                        }
-                        const uint32_t row = (uint32_t)(nl * 32 + s);
-                        *reinterpret_cast<uint4*>(Bs + ce_sw64(row, c)) = ce_onehot_chunk(sl, (uint32_t)s, one);
-                    }
-                    // each output's largest present exponent sum and signed present count
-                    for (int i = tb; i < 2 * 32; i += CE_BUILDERS) {
-                        const int h = i >> 5, o = i & 31, ml = o >> 3, nl = o & 7;
-                        const int64_t g = 2 * gp + h;
-                        int pe = -16384, pn = 0;
-                        if (g < G) {
-                            const int64_t ra = g * A.pitch + m0 + ml, rb = g * B.pitch + nt + nl;
-                            uint32_t e2 = 0xC000C000u;
+            }
+            const uint32_t ubuf = (uint32_t)(u & 1u), uph = (uint32_t)((u >> 1) & 1u);
+            ok = ce_wait(&b_empty[ubuf], uph ^ 1u, abort_flag, LIMIT, 5);
+            if (!ok) break;
+            unsigned char* Bs = smem + CE_OFF_B + ubuf * CE_B_BYTES;
+            // one-hot weight slot rows carrying the class sign
+            for (int i = tb; i < 256 * 4; i += CE_BUILDERS) {
+                const uint32_t row = (uint32_t)(i >> 2), c = (uint32_t)(i & 3);
+                const uint32_t h = c >> 1, nl = row >> 5, sl_i = row & 31u;
+                uint4 sl = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+                uint32_t one = 1u;
+                if (2 * gp + h < G) {
+                    sl = *reinterpret_cast<const uint4*>(SLB + (h * CE_TN + nl) * 32 + (c & 1u) * 16);
+                    one = ((PSB[h * CE_TN + nl].z >> sl_i) & 1u) ? 0xFFu : 1u;
+                }
+                *reinterpret_cast<uint4*>(Bs + ce_sw64(row, c)) = ce_onehot_chunk(sl, sl_i, one);
+            }
+            // class magnitudes and fingerprint weights of the 256 slot columns, both groups
+            for (int i = tb; i < 2 * 256; i += CE_BUILDERS) {
+                const int h = i >> 8, col = i & 255;
+                const uint32_t code = 2 * gp + h < G ? CTB[(h * CE_TN + (col >> 5)) * 32 + (col & 31)] : 0u;
+                FB[(ubuf * 2 + h) * 256 + col] = ce_magnitude(code);
+                RR[(ubuf * 2 + h) * 256 + col] = ce_fingerprint_weight(P.seed, u * 2 + h, (uint32_t)col);
+            }
+            // each output's largest present exponent sum and signed present count
+            for (int i = tb; i < 2 * 32; i += CE_BUILDERS) {
+                const int h = i >> 5, o = i & 31, ml = o >> 3, nl = o & 7;
+                int pe = -16384, pn = 0;
+                if (2 * gp + h < G) {
+                    const uint32_t* ea = EXA + (h * CE_TM + ml) * 16;
+                    const uint32_t* eb = EXB + (h * CE_TN + nl) * 16;
+                    uint32_t e2 = 0xC000C000u;
 #pragma unroll
-                            for (int j = 0; j < 16; ++j) e2 = __viaddmax_s16x2(A.ex[ra * 16 + j], B.ex[rb * 16 + j], e2);
-                            pe = max((int)(int16_t)(e2 & 0xFFFFu), (int)(int16_t)(e2 >> 16));
-                            const uint4 pa = A.ps[ra], pb = B.ps[rb];
-                            const uint32_t both = pa.x & pb.x;
-                            pn = __popc(both) - 2 * __popc(both & (pa.y ^ pb.y));
-                        }
-                        PE[(ubuf * 2 + h) * 32 + o] = pe;
-                        PN[(ubuf * 2 + h) * 32 + o] = pn;
+                    for (int j = 0; j < 16; ++j) e2 = __viaddmax_s16x2(ea[j], eb[j], e2);
+                    pe = max((int)(int16_t)(e2 & 0xFFFFu), (int)(int16_t)(e2 >> 16));
+                    const uint4 pa = PSA[h * CE_TM + ml], pb = PSB[h * CE_TN + nl];
+                    const uint32_t both = pa.x & pb.x;
+                    pn = __popc(both) - 2 * __popc(both & (pa.y ^ pb.y));
+                }
+                PE[(ubuf * 2 + h) * 32 + o] = pe;
+                PN[(ubuf * 2 + h) * 32 + o] = pn;
+            }
+            // B^T r per k: the weight side of the fingerprint, two int8 vectors for each half of
+            // the tile's weight rows (an epilogue warp sees the columns of one half); the weights
+            // are recomputed from their hash rather than read back from RR, so the builders need
+            // no barrier among themselves
+            for (int i = tb; i < 2 * 2 * 32; i += CE_BUILDERS) {
+                const int h = i >> 6, half = (i >> 5) & 1, k = i & 31;
+                int s1 = 0, s2 = 0;
+                if (2 * gp + h < G) {
+#pragma unroll
+                    for (int nl = half * 4; nl < half * 4 + 4; ++nl) {
+                        const uint32_t slot = SLB[(h * CE_TN + nl) * 32 + k];
+                        if (slot == CE_NO_SLOT) continue;
+                        const uint32_t rr = ce_fingerprint_weight(P.seed, u * 2 + h, (uint32_t)(nl * 32 + slot));
+                        const bool neg = (PSB[h * CE_TN + nl].z >> slot) & 1u;
+                        s1 += neg ? -(int)(rr & 0xFFFFu) : (int)(rr & 0xFFFFu);
+                        s2 += neg ? -(int)(rr >> 16) : (int)(rr >> 16);
                     }
-                    // B^T r per k: the weight side of the fingerprint, two int8 vectors for
-                    // each half of the tile's weight rows (an epilogue warp sees the columns of
-                    // one half); the weights are recomputed from their hash rather than read
-                    // back from RR, so the builders need no barrier among themselves
-                    for (int i = tb; i < 2 * 2 * 32; i += CE_BUILDERS) {
-                        const int h = i >> 6, half = (i >> 5) & 1, k = i & 31;
-                        const int64_t g = 2 * gp + h;
-                        int s1 = 0, s2 = 0;
-                        if (g < G) {
-                            for (int nl = half * 4; nl < half * 4 + 4; ++nl) {
-                                const int64_t rec = g * B.pitch + nt + nl;
-                                const uint32_t slot = B.sl[rec * 32 + k];
-                                if (slot == CE_NO_SLOT) continue;
-                                const uint32_t rr = ce_fingerprint_weight(P.seed, unit * 2 + h, (uint32_t)(nl * 32 + slot));
-                                const bool neg = (B.ps[rec].z >> slot) & 1u;
-                                s1 += neg ? -(int)(rr & 0xFFFFu) : (int)(rr & 0xFFFFu);
-                                s2 += neg ? -(int)(rr >> 16) : (int)(rr >> 16);
-                            }
-                        }
-                        BR[(((ubuf * 2 + h) * 2 + half) * 2 + 0) * 32 + k] = (int8_t)s1;
-                        BR[(((ubuf * 2 + h) * 2 + half) * 2 + 1) * 32 + k] = (int8_t)s2;
-                    }
-                    fence_proxy_async_smem();
-                    mbar_arrive(&b_full[ubuf]);
+                }
+                BR[(((ubuf * 2 + h) * 2 + half) * 2 + 0) * 32 + k] = (int8_t)s1;
+                BR[(((ubuf * 2 + h) * 2 + half) * 2 + 1) * 32 + k] = (int8_t)s2;
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&b_full[ubuf]);
+            mbar_arrive(&s_empty[sbuf]);
+            ++u;
+            ce_cursor_next(cur, P, strips, GP);
+        }
+        if (loader) {
+            // drain: every staging copy issued has landed before the CTA can exit
+            for (uint64_t b = 0; b < 2; ++b) {
+                if (issued > b) {
+                    const uint64_t last = issued - 1 - ((issued - 1 - b) & 1u);   // last unit staged into buffer b
+                    mbar_wait_bounded(&s_full[b], (uint32_t)((last >> 1) & 1u), CE_WHERE, 12);
                 }
             }
         }
@@ -423,16 +564,16 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
             for (int64_t gp = 0; gp < GP && ok; ++gp) {
                 const uint32_t abuf = a_cnt & 1u, aph = (a_cnt >> 1) & 1u;
                 ++a_cnt;
-                ok = mbar_wait_or_abort(&a_full[abuf], aph, abort_flag, LIMIT, CE_WHERE, 6);
+                ok = ce_wait(&a_full[abuf], aph, abort_flag, LIMIT, 6);
                 if (!__all_sync(FULL, ok)) { ok = false; break; }
                 for (int t = 0; t < tiles && ok; ++t) {
                     const uint32_t ubuf = u_cnt & 1u, uph = (u_cnt >> 1) & 1u, tph = u_cnt & 1u;
                     ++u_cnt;
-                    ok = mbar_wait_or_abort(&b_full[ubuf], uph, abort_flag, LIMIT, CE_WHERE, 7);
+                    ok = ce_wait(&b_full[ubuf], uph, abort_flag, LIMIT, 7);
                     if (!__all_sync(FULL, ok)) { ok = false; break; }
                     for (int h = 0; h < 2; ++h) {
                         const int64_t g = 2 * gp + h;
-                        ok = mbar_wait_or_abort(&t_full[h], tph, abort_flag, LIMIT, CE_WHERE, 8);
+                        ok = ce_wait(&t_full[h], tph, abort_flag, LIMIT, 8);
                         __syncwarp();
                         if (!__all_sync(FULL, ok)) { ok = false; break; }
                         tc_fence_after();
@@ -452,43 +593,45 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                         const int64_t tile_id = (((sid * GP + gp) * CE_MAX_TILES + t) * 2 + h);
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            const int col0 = (4 * hn + i) * 32;
-                            uint32_t c[32];
-                            if (P.tiles_in) {
-                                const int4* src = reinterpret_cast<const int4*>(P.tiles_in + (tile_id * 128 + row) * 256 + col0);
-#pragma unroll
-                                for (int v = 0; v < 8; ++v) {
-                                    const int4 x = src[v];
-                                    c[4 * v] = (uint32_t)x.x; c[4 * v + 1] = (uint32_t)x.y;
-                                    c[4 * v + 2] = (uint32_t)x.z; c[4 * v + 3] = (uint32_t)x.w;
-                                }
-                            } else {
-                                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + col0);
-                                uint32_t (&lo)[16] = *reinterpret_cast<uint32_t(*)[16]>(&c[0]);
-                                uint32_t (&hi)[16] = *reinterpret_cast<uint32_t(*)[16]>(&c[16]);
-                                tmem_ld16(taddr, lo);
-                                tmem_ld16(taddr + 16, hi);
-                                tmem_wait_ld();
-                            }
-                            if (P.tiles_out) {
-                                int4* dst = reinterpret_cast<int4*>(P.tiles_out + (tile_id * 128 + row) * 256 + col0);
-#pragma unroll
-                                for (int v = 0; v < 8; ++v)
-                                    dst[v] = make_int4((int)c[4 * v], (int)c[4 * v + 1], (int)c[4 * v + 2], (int)c[4 * v + 3]);
-                            }
                             const float msf = __uint_as_float(ms[i]);
-                            const float4* fb4 = reinterpret_cast<const float4*>(FB + tb * 256 + col0);
-                            const uint4* rr4 = reinterpret_cast<const uint4*>(RR + tb * 256 + col0);
                             uint32_t acc_i = 0;
 #pragma unroll
-                            for (int v = 0; v < 8; ++v) {
-                                const float4 fb = fb4[v];
-                                const uint4 rr = rr4[v];
-                                acc_i += c[4 * v] * __float_as_uint(__fmaf_rz(fa_abs, fb.x, msf));
-                                acc_i += c[4 * v + 1] * __float_as_uint(__fmaf_rz(fa_abs, fb.y, msf));
-                                acc_i += c[4 * v + 2] * __float_as_uint(__fmaf_rz(fa_abs, fb.z, msf));
-                                acc_i += c[4 * v + 3] * __float_as_uint(__fmaf_rz(fa_abs, fb.w, msf));
-                                fp += c[4 * v] * rr.x + c[4 * v + 1] * rr.y + c[4 * v + 2] * rr.z + c[4 * v + 3] * rr.w;
+                            for (int half = 0; half < 2; ++half) {
+                                // 16 count columns (weight row 4 hn + i, slots 16 half ..) per pass
+                                const int col0 = (4 * hn + i) * 32 + half * 16;
+                                uint32_t c[16];
+                                if constexpr (MODE == CE_SUPPLIED_TILES) {
+                                    const int4* src =
+                                        reinterpret_cast<const int4*>(P.tiles_in + (tile_id * 128 + row) * 256 + col0);
+#pragma unroll
+                                    for (int v = 0; v < 4; ++v) {
+                                        const int4 x = src[v];
+                                        c[4 * v] = (uint32_t)x.x; c[4 * v + 1] = (uint32_t)x.y;
+                                        c[4 * v + 2] = (uint32_t)x.z; c[4 * v + 3] = (uint32_t)x.w;
+                                    }
+                                } else {
+                                    tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + col0), c);
+                                    tmem_wait_ld();
+                                }
+                                if constexpr (MODE == CE_DUMP_TILES) {
+                                    int4* dst = reinterpret_cast<int4*>(P.tiles_out + (tile_id * 128 + row) * 256 + col0);
+#pragma unroll
+                                    for (int v = 0; v < 4; ++v)
+                                        dst[v] = make_int4((int)c[4 * v], (int)c[4 * v + 1], (int)c[4 * v + 2],
+                                                           (int)c[4 * v + 3]);
+                                }
+                                const float4* fb4 = reinterpret_cast<const float4*>(FB + tb * 256 + col0);
+                                const uint4* rr4 = reinterpret_cast<const uint4*>(RR + tb * 256 + col0);
+#pragma unroll
+                                for (int v = 0; v < 4; ++v) {
+                                    const float4 fb = fb4[v];
+                                    const uint4 rr = rr4[v];
+                                    acc_i += c[4 * v] * __float_as_uint(__fmaf_rz(fa_abs, fb.x, msf));
+                                    acc_i += c[4 * v + 1] * __float_as_uint(__fmaf_rz(fa_abs, fb.y, msf));
+                                    acc_i += c[4 * v + 2] * __float_as_uint(__fmaf_rz(fa_abs, fb.z, msf));
+                                    acc_i += c[4 * v + 3] * __float_as_uint(__fmaf_rz(fa_abs, fb.w, msf));
+                                    fp += c[4 * v] * rr.x + c[4 * v + 1] * rr.y + c[4 * v + 2] * rr.z + c[4 * v + 3] * rr.w;
+                                }
                             }
                             part[i] = acc_i;
                         }
@@ -623,8 +766,10 @@ int ima_class_count_replay(const void* x_operand, const void* w_operand, const f
     p.tiles_in = tiles_in;
     p.seed = seed;
     const int64_t strips = p.strips_m * p.strips_n;
-    int rc = ima_note_cuda(
-        cudaFuncSetAttribute(class_count_replay_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CE_ALLOC));
+    if (tiles_out && tiles_in) return IMA_ERR_INVALID_ARGUMENT;
+    auto kern = tiles_in ? class_count_replay_kernel<CE_SUPPLIED_TILES>
+                         : tiles_out ? class_count_replay_kernel<CE_DUMP_TILES> : class_count_replay_kernel<CE_TENSOR_COUNTS>;
+    int rc = ima_note_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CE_ALLOC));
     if (rc != IMA_OK) return rc;
     if (K == 0) {
         // no products: every output is the zero accumulator
@@ -634,7 +779,7 @@ int ima_class_count_replay(const void* x_operand, const void* w_operand, const f
         return rc;
     }
     const int grid = (int)(strips < num_sms() ? strips : num_sms());
-    class_count_replay_kernel<<<grid, CE_THREADS, CE_ALLOC, (cudaStream_t)stream>>>(p);
+    kern<<<grid, CE_THREADS, CE_ALLOC, (cudaStream_t)stream>>>(p);
     return IMA_LAUNCH_STATUS();
 }
 
