@@ -1,23 +1,24 @@
 """Benchmark of the B200 student-linear hot path (prints ONE JSON line on rank 0).
 
-Workload (N = 1 GPU): configuration 1 -- all 168 FP8 linears of a random-init
-Qwen2.5-0.5B-shaped model, 512 tokens each, codebook student: per-token e4m3
-quantisation, the exact int64 GEMM (tcgen05 kind::i8, fused rescale/bias/bf16
-epilogue) with full int64 outputs, and a Freivalds check of every product.
-A "step" is one forward of all 168 linears.  Metric: exact int GEMM TOPS =
-sum over linears of 2*M*N*K / step time (whole job, all GPUs).
+Headline workload, at every GPU count (python bench.py --gpus N, one process per GPU under
+torchrun for N > 1): configuration 4 -- the 196 FP8 linears of a random-init
+Qwen2.5-7B-shaped model at 16384 tokens, codebook student: per-token e4m3 quantisation, the
+exact int64 GEMM (tcgen05 kind::i8, fused rescale/bias/bf16 epilogue) with full int64
+outputs, a Freivalds check of every product, and the bf16 outputs gathered to every GPU.
+The tokens are split over the GPUs by rows, gate/up by output columns (strong scaling).  A
+"step" is one forward of all 196 linears.  Metric: exact int GEMM TOPS = sum over linears of
+2*M*N*K / step time (whole job, max over ranks).  Every N also reports config 4 through the
+direct Hawkeye replay ("c4_hawkeye").
 
-At N = 1 the line also carries "hawkeye_c2": the config-2 measurement (all 168 linears at
-16384 tokens through the direct Hawkeye replay; outputs/s, products/s, INT-issue roofline).
+At N = 1 the line also carries "c1" (the 168 Qwen2.5-0.5B-shaped linears at 512 tokens, with
+its pipelined and per-linear-plugin end-to-end loops), "hawkeye_c2" (the 0.5B linears at 16384
+tokens through the Hawkeye replay) and "class_counts_c3" (the class-count engine on the
+down_proj shape).  --c1-only, --hawkeye-only and --class-counts-only run one of those alone;
+--profile-step / --profile-c4 run two eager forwards for ncu captures.
 
-N > 1 (torchrun): every rank runs the same workload on its own token batch (weak
-scaling); the only collective is an all-reduce of the Freivalds mismatch counter.
-
---config4 runs the config-4 (Qwen2.5-7B shapes, 16384 tokens) multi-GPU measurement,
---hawkeye-only the config-2 measurement alone.
-
---impl reference times the reference's CPU path (its torch expressions: per-token
-quantiser, torch int64 matmul, fp32 rescale) on the host cores over a bounded sample.
+--impl reference times the reference's CPU formulation of the codebook path (its torch
+quantiser expressions, torch int64 matmul, fp32 rescale) on the host cores over a bounded
+sample of the same workload.
 """
 
 from __future__ import annotations
@@ -38,7 +39,8 @@ sys.path.insert(0, ROOT)
 
 TOKENS = 512
 # the metric both arms report (the driver compares the lines)
-METRIC = "exact int GEMM TOPS (bit-exact codebook int64 GEMM + fused rescale + Freivalds check)"
+METRIC = ("exact int GEMM TOPS (bit-exact codebook int64 GEMM + fused rescale + Freivalds check of every "
+          "product; config 4: 196 Qwen2.5-7B-shaped linears, 16384 tokens)")
 
 
 def _dist():
@@ -289,12 +291,14 @@ def run_hawkeye(args, emit: bool = True) -> dict:
 def run_class_counts_c3(args) -> dict:
     """Config 3: the hawkeye-class-counts student on the down_proj shape (M = 4096, K = 4864,
     N = 896) with class_chunk 512, 6 packed count lanes and 2 packed group lanes, through
-    exact_hawkeye_fp8_sum with this package's _int32_raw_matmul (what
-    HawkeyeClassCountsLinear passes): the per-pack class presence for the stats, then the
-    output from the direct replay.  Each call reads the stats back to the host (as the
-    reference's does), so each timed call is bracketed by CUDA events on an otherwise idle
-    stream.  The output is compared with the direct replay once, outside the timing."""
-    from int_model_approximation_b200 import codebook, hawkeye, hawkeye_freivalds, students, synthetic
+    exact_hawkeye_fp8_sum with raw_matmul None (what HawkeyeClassCountsLinear passes): the
+    per-pack class presence for the stats, then the class-count engine -- count products
+    formed on the tensor cores, every count tile fingerprinted, the accumulator replayed from
+    the counts.  Each call reads the stats and the fingerprint verdict back to the host (as
+    the reference reads its class lists), so each timed call is bracketed by CUDA events on
+    an otherwise idle stream.  The engine kernel alone (operands staged) is timed the same
+    way for its tensor-pipe fraction."""
+    from int_model_approximation_b200 import codebook, hawkeye, hawkeye_freivalds, synthetic
 
     device = torch.device("cuda", 0)
     shape = synthetic.LinearShape("down_proj", 896, 4864)
@@ -303,7 +307,7 @@ def run_class_counts_c3(args) -> dict:
     params = dict(class_chunk=512, packed_count_lanes=6, packed_group_lanes=2)
 
     def call():
-        return hawkeye_freivalds.exact_hawkeye_fp8_sum(xq, xs, w, ws, students._int32_raw_matmul, **params)
+        return hawkeye_freivalds.exact_hawkeye_fp8_sum(xq, xs, w, ws, None, **params)
 
     y, stats = call()
     direct, _ = hawkeye.hawkeye_fp8_sum(xq, xs, w, ws)
@@ -312,41 +316,92 @@ def run_class_counts_c3(args) -> dict:
         call()
     torch.cuda.synchronize()
     steps = 5
-    total_ms = 0.0
     stream = torch.cuda.current_stream(device)
-    for _ in range(steps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        call()
-        b.record(stream)
-        b.synchronize()
-        total_ms += a.elapsed_time(b)
-    ms = total_ms / steps
+
+    def timed(fn) -> float:
+        total = 0.0
+        for _ in range(steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            b.synchronize()
+            total += a.elapsed_time(b)
+        return total / steps
+
+    ms = timed(call)
+    # the engine kernel alone on staged operands
+    x_op = hawkeye_freivalds.ClassCountOperand(xq)
+    w_op = hawkeye_freivalds.stage_class_count_weight(w)
+    mism = torch.zeros((1,), dtype=torch.int32, device=device)
+    out = torch.empty_like(y)
+    xs32 = xs.reshape(-1).to(torch.float32).contiguous()
+    ws32 = ws.reshape(-1).to(torch.float32).contiguous()
+
+    def engine():
+        hawkeye_freivalds.class_count_replay(x_op, w_op, xs32, ws32, out=out, mismatch=mism)
+
+    engine()
+    torch.cuda.synchronize()
+    mism.zero_()
+    kernel_ms = timed(engine)
+    fingerprint_failures = int(mism.item())
     m, n, k = int(x.shape[0]), shape.n, shape.k
+    groups = -(-k // 32)
+    tiles = -(-m // 4) * sum(min(8, -(-(n - n0) // 8)) for n0 in range(0, n, 64)) * 2 * (-(-groups // 2))
+    count_macs = tiles * 128 * 256 * 32          # MACs the engine's MMAs perform (one 128x256x32 MMA per tile)
+    peak, peak_source = int8_tensor_peak()
+    # the reference's count products for the same stats: per pack (n_a M) x 64 x (ceil(n_b / 3) N)
+    a_cnt = hawkeye_freivalds._popcounts(hawkeye_freivalds.class_presence(xq, 64))
+    b_cnt = hawkeye_freivalds._popcounts(hawkeye_freivalds.class_presence(w, 64))
+    ref_macs = sum(na * m * 64 * (-(-nb // 3)) * n for na, nb in zip(a_cnt, b_cnt))
     res = {
         "workload": "c3: down_proj 4096 x 4864 -> 896, hawkeye-class-counts, class_chunk 512, "
                     "6 count lanes, 2 group lanes",
         "outputs_per_s": m * n / (ms * 1e-3),
         "products_per_s": m * n * k / (ms * 1e-3),
         "ms_per_call": round(ms, 4),
+        "engine_kernel_ms": round(kernel_ms, 4),
         "steps": steps,
         "equals_direct_replay": equal,
+        "fingerprint_failed_rows": fingerprint_failures,
         "stats": {key: val for key, val in stats.__dict__.items()},
-        "note": "the checkable count products are folded into the replay, not formed: "
-                "total_checkable_products is the number the reference would send through its int GEMM",
+        "count_products": {
+            "formed_by": "class_count_replay_kernel: one tcgen05.mma kind::i8 (128 x 256 x 32) per tile of 4 "
+                         "tokens x 8 weight rows x 32 class slots each, per group of 32 k",
+            "mma_tiles_per_call": tiles,
+            "count_macs_per_call": count_macs,
+            "count_macs_per_s": count_macs / (kernel_ms * 1e-3),
+            "count_entries_replayed_per_call": tiles * 128 * 256,
+            "reference_count_macs_per_call": ref_macs,
+            "reference_products_per_call": stats.total_checkable_products,
+        },
+        "roofline": {
+            "kernel": "class_count_replay_kernel",
+            "bound": "epilogue instruction issue (every count entry is replayed: FFMA.RZ + 2 IMAD); "
+                     "the tensor pipe forms the counts",
+            "achieved": round(2.0 * count_macs / (kernel_ms * 1e-3) / 1e12, 2),
+            "peak": round(peak, 1) if peak else None,
+            "unit": "TOPS (int8 tensor ops of the count MMAs)",
+            "frac": round(2.0 * count_macs / (kernel_ms * 1e-3) / 1e12 / peak, 4) if peak else None,
+            "peak_source": peak_source,
+        },
     }
     if not args.no_cpu_baseline:
         import oracle
 
         rows = 128
         t0 = time.perf_counter()
-        oracle.hawkeye(xq[:rows].cpu(), xs[:rows].cpu(), w.cpu(), ws.cpu())
+        ref = oracle.hawkeye(xq[:rows].cpu(), xs[:rows].cpu(), w.cpu(), ws.cpu())
         t = time.perf_counter() - t0
         res["cpu_baseline"] = {
             "value": rows * n * k / t, "unit": "products/s", "cores": max(1, min(32, os.cpu_count() or 1)),
             "kind": "port",
             "sample": f"{rows} token rows through the oracle's C restatement of the replay (the output equals "
                       f"the direct replay), {t:.1f} s",
+            "parity": {"rows_checked": rows, "ok": bool(torch.equal(y[:rows].cpu().view(torch.int16),
+                                                                    ref.to(torch.bfloat16).view(torch.int16))),
+                       "what": "the engine's bf16 rows vs the CPU replay, bit for bit"},
         }
     return res
 
@@ -408,14 +463,39 @@ def run_profile_step(args) -> None:
     print(json.dumps({"profile_step": "done", "mismatch": int(bufs["mismatch"].item())}))
 
 
-def run_b200(args) -> None:
-    world, rank, local = _dist()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        import datetime
+def run_profile_c4(args) -> None:
+    """Two eager forwards of the first `--c4-layers` layers of config 4 at N = 1 (one grouped
+    quantiser, GEMM and check launch per layer): the command profiled by ncu for the c4 GEMM's
+    DRAM traffic (its second forward's launches are the captured ones)."""
+    from int_model_approximation_b200.codebook import DigitPlanes  # noqa: F401
+    from int_model_approximation_b200.pipeline import CodebookStack
 
-        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    specs = c4_specs(args.c4_tokens, 1, 0)
+    xs = c4_inputs(specs, args.c4_tokens, device)
+    stacks = [CodebookStack([c4_weights(sp, layer, p, device) for p, sp in enumerate(specs)], seed=layer)
+              for layer in range(args.c4_layers)]
+    bufs = stacks[0].allocate(args.c4_tokens)
+    views = [dict(bufs) for _ in stacks]
+    # this stack mixes token counts per linear (gate/up keep all tokens), so allocate per linear
+    for v in views:
+        for key in ("q", "scale", "code_scale", "planes", "c", "y"):
+            v[key] = list(bufs[key])
+    for _ in range(2):
+        for st, v in zip(stacks, views):
+            st.forward(xs, v)
+        torch.cuda.synchronize()
+    print(json.dumps({"profile_c4": "done", "layers": args.c4_layers, "mismatch": int(bufs["mismatch"].item())}))
+
+
+def run_c1(args) -> dict:
+    """Config 1 on one GPU (returned as the "c1" object of the default line): all 168 linears of
+    the 0.5B shapes at 512 tokens, codebook student with int64 outputs and a Freivalds check of
+    every product; exact TOPS, the GEMM roofline, the pipelined end-to-end loop, the per-linear
+    plugin loop and the CPU baseline with parity of the timed outputs."""
+    world, rank, local = 1, 0, 0
+    device = torch.device("cuda", local)
     from int_model_approximation_b200 import _native as nat
     from int_model_approximation_b200.pipeline import CodebookStack
 
@@ -694,22 +774,8 @@ def run_b200(args) -> None:
             "cpu_baseline": cpu,
             "measured_peaks": {k: peaks.get(k) for k in ("hbm_gbs", "bf16_tflops")},
         }
-        if world == 1 and not args.no_hawkeye:
-            # the other half of the metric: config-2 Hawkeye replay outputs/s (a failure here
-            # is reported in the line and does not cost the codebook measurement)
-            try:
-                line["hawkeye_c2"] = run_hawkeye(args, emit=False)
-            except Exception as exc:  # noqa: BLE001
-                line["hawkeye_c2"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
-        if world == 1 and not args.no_class_counts:
-            try:
-                line["class_counts_c3"] = run_class_counts_c3(args)
-            except Exception as exc:  # noqa: BLE001
-                line["class_counts_c3"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        del graph, phase_graphs
-        torch.distributed.destroy_process_group()
+        return line
+    return {}
 
 
 def plugin_e2e(weights, xs, steps: int, device) -> dict:
@@ -809,34 +875,41 @@ def cpu_baseline_sample(shapes, weights, xs, budget_s: float = 15.0, gpu_c=None,
 
 
 def run_reference(args) -> None:
+    """The reference arm: the reference's own CPU formulation of the codebook path (its torch
+    quantiser expressions, torch int64 matmul in place of its Triton kernel, fp32 rescale, bias;
+    oracle.torch_cpu_codebook_linear) on the host cores, on the B200 arm's workload (config 4),
+    each step one linear of the 7B-shaped model with `--reference-rows` token rows, cycling
+    through the seven shapes of successive layers; rows split over every host thread.  Under
+    torchrun only rank 0 runs it."""
     world, rank, _local = _dist()
     if rank != 0:
         return
-    from int_model_approximation_b200 import synthetic
     import oracle
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(1)   # one row part per host thread (torch's int64 matmul is single-threaded)
-    shapes = synthetic.config_linears(1)
+    specs = c4_specs(args.c4_tokens, 1, 0)
     rows = args.reference_rows
 
     def sample(i):
-        s = shapes[i % len(shapes)]
-        seed = synthetic.linear_seed(1, i % len(shapes))
-        x = synthetic.student_t_activations(rows, s.k, seed)
-        w, ws = synthetic.normal_fp8_weights(s.n, s.k, seed + 500_000)
-        return s, x, w, ws, oracle.fp8_codebook(w).to(torch.int64)   # weight prepack: once per linear
+        layer, p = (i // 7) % args.c4_layers, i % 7
+        sp = specs[p]
+        from int_model_approximation_b200 import synthetic
+
+        x = synthetic.student_t_activations(rows, sp["k"], synthetic.linear_seed(4, p))
+        w, ws, bias = c4_weights(sp, layer, p, "cpu")
+        return sp, x, w, ws, bias, oracle.fp8_codebook(w).to(torch.int64)   # weight prepack: once per linear
 
     for i in range(args.warmup):
-        s, x, w, ws, codes = sample(i)
-        oracle.torch_cpu_codebook_linear(x, w, ws, None, threads=threads, w_codes=codes)
+        sp, x, w, ws, bias, codes = sample(i)
+        oracle.torch_cpu_codebook_linear(x, w, ws, bias, threads=threads, w_codes=codes)
     total_t, total_ops = 0.0, 0.0
     for i in range(args.steps):
-        s, x, w, ws, codes = sample(args.warmup + i)
+        sp, x, w, ws, bias, codes = sample(args.warmup + i)
         t0 = time.perf_counter()
-        oracle.torch_cpu_codebook_linear(x, w, ws, None, threads=threads, w_codes=codes)
+        oracle.torch_cpu_codebook_linear(x, w, ws, bias, threads=threads, w_codes=codes)
         total_t += time.perf_counter() - t0
-        total_ops += 2.0 * rows * s.n * s.k
+        total_ops += 2.0 * rows * sp["n"] * sp["k"]
     value = total_ops / total_t / 1e12
     line = {
         "impl": "reference",
@@ -848,40 +921,91 @@ def run_reference(args) -> None:
         "warmup": args.warmup,
         "ms_per_step": round(total_t / args.steps * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int64",
         "data": "synthetic",
-        "config": {"workload": "c1: 168 FP8 linears of Qwen2.5-0.5B shape, codebook student",
+        "config": {"workload": "c4: 196 FP8 linears of Qwen2.5-7B shape, codebook student (the reference's CPU "
+                               "formulation)",
                    "sample_rows_per_step": rows,
                    "freivalds": "not timed: the reference checks its products only in its tests"},
         "cpu_baseline": {"value": round(value, 6), "unit": "TOPS", "cores": threads, "kind": "port",
-                         "sample": f"one whole linear per step ({rows} token rows, as in the workload, split "
-                                   f"over {threads} threads), cycling through the 168 linears"},
+                         "sample": f"one linear per step ({rows} token rows split over {threads} threads), cycling "
+                                   f"through the seven 7B shapes of successive layers"},
         "e2e": {"value": round(value, 6), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_c4(args) -> None:
-    """Config 4: the 196 FP8 linears of a Qwen2.5-7B-shaped model at `--c4-tokens` tokens
-    (16384), split over the ranks by token rows with the weights replicated, except
-    gate_proj/up_proj, whose weights are split by output columns (every rank then holds all
-    tokens for them).  Phase "codebook": per layer, the grouped quantiser, the exact int64
-    GEMM with the fused rescale and the Freivalds row check of every local product, then one
-    NCCL all-gather per linear of the bf16 output shards.  Phase "hawkeye": per linear,
-    quantise, stage and replay, then the same gathers.  Gathers run on a second stream and
-    overlap the next layer's compute (two output buffer sets alternate).  The seven
-    activation matrices of a layer are shared by all 28 layers (synthetic inputs of the
-    right shapes; the work per layer is unchanged), so memory stays within one GPU at N = 1.
-    Each phase is timed on the device (CUDA events, max over ranks)."""
-    import datetime
+C4_METRIC = METRIC
 
-    from int_model_approximation_b200 import _native as nat
+
+def c4_specs(tokens: int, world: int, rank: int) -> list[dict]:
+    """This rank's share of each of the seven linears of a layer: token rows for q/k/v/o/down,
+    output columns (all tokens) for gate/up."""
     from int_model_approximation_b200 import sharding, synthetic
-    from int_model_approximation_b200.codebook import DigitPlanes
-    from int_model_approximation_b200.hawkeye import HawkeyeOperand
-    from int_model_approximation_b200.pipeline import CodebookStack
+
+    specs = []
+    for s in synthetic.qwen_layer_shapes(3584, 512, 18944):
+        if s.name in ("gate_proj", "up_proj"):
+            c0, c1 = sharding.col_shard(s.n, world, rank)
+            if (c1 - c0) * world != s.n:
+                raise SystemExit(f"{s.name}: {s.n} columns do not split evenly over {world} GPUs")
+            specs.append(dict(name=s.name, k=s.k, n=c1 - c0, n_full=s.n, rows=tokens, col=True, col0=c0))
+        else:
+            r0, r1 = sharding.row_shard(tokens, world, rank)
+            specs.append(dict(name=s.name, k=s.k, n=s.n, n_full=s.n, rows=r1 - r0, col=False, row0=r0))
+    return specs
+
+
+def c4_weight_seed(layer: int, p: int) -> int:
+    from int_model_approximation_b200 import synthetic
+
+    return synthetic.linear_seed(4, 7 * layer + p) + 500_000
+
+
+def c4_weights(spec: dict, layer: int, p: int, device):
+    """(w_fp8 [n, K], w_scale [n, 1], bias bf16 [n]) of this rank's share of linear (layer, p): the
+    full weight is drawn from its seed and the rank keeps its output columns (gate/up), so
+    every rank computes exactly its part of the same model."""
+    from int_model_approximation_b200 import synthetic
+
+    w, ws = synthetic.normal_fp8_weights(spec["n_full"], spec["k"], c4_weight_seed(layer, p), device=device)
+    g = torch.Generator(device=device).manual_seed(c4_weight_seed(layer, p) + 77)
+    bias = (torch.randn(spec["n_full"], generator=g, device=device) * 0.01).to(torch.bfloat16)
+    if spec["col"]:
+        c0, c1 = spec["col0"], spec["col0"] + spec["n"]
+        return w[c0:c1].contiguous(), ws[c0:c1].contiguous(), bias[c0:c1].contiguous()
+    return w, ws, bias
+
+
+def c4_inputs(specs: list[dict], tokens: int, device) -> list[torch.Tensor]:
+    """The seven activation matrices of a layer (shared by the 28 layers: synthetic inputs of
+    the right shapes; the work per layer is unchanged), this rank's rows of each."""
+    from int_model_approximation_b200 import synthetic
+
+    xs = []
+    for p, sp in enumerate(specs):
+        x = synthetic.student_t_activations(tokens, sp["k"], synthetic.linear_seed(4, p), device=device)
+        xs.append(x if sp["col"] else x[sp["row0"]:sp["row0"] + sp["rows"]].contiguous())
+    return xs
+
+
+def run_headline(args) -> None:
+    """The default measurement: config 4 -- the 196 FP8 linears of a Qwen2.5-7B-shaped model at
+    16384 tokens -- on N GPUs (one process per GPU under torchrun), partitioned as BASELINE's
+    north star says: token rows over the ranks with the weights replicated, gate/up split by
+    output columns (every rank holds all tokens for them), and the bf16 outputs gathered to
+    every rank.  A step is one forward of all 196 linears: per layer the grouped quantiser,
+    the exact int64 GEMM with the fused rescale (one grouped launch), the gathers of its
+    outputs (peer-to-peer copies on the copy engines, started as soon as the GEMM has written
+    them) and the Freivalds row check of every local int64 product.  Strong scaling: the
+    16384 tokens are fixed.  value = exact int ops of the whole model / step time (max over
+    ranks).  At N = 1 the line also carries config 1 (the 0.5B codebook stack), config 2
+    (Hawkeye replay) and config 3 (class counts); at every N it carries config 4's Hawkeye
+    replay phase."""
+    import ctypes
+    import datetime
 
     world, rank, local = _dist()
     device = torch.device("cuda", local)
@@ -889,36 +1013,21 @@ def run_c4(args) -> None:
     dist = torch.distributed
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=600))
+    from int_model_approximation_b200 import _native as nat
+    from int_model_approximation_b200 import synthetic
+    from int_model_approximation_b200.codebook import DigitPlanes
+    from int_model_approximation_b200.pipeline import CodebookStack
+
     lib = nat.lib()
     tokens, layers = args.c4_tokens, args.c4_layers
-    phases = [p for p in args.c4_phases.split(",") if p]
     if tokens % world:
         raise SystemExit("--c4-tokens must be a multiple of the number of GPUs")
-    specs = []
-    for p, s in enumerate(synthetic.qwen_layer_shapes(3584, 512, 18944)):
-        if s.name in ("gate_proj", "up_proj"):
-            c0, c1 = sharding.col_shard(s.n, world, rank)
-            if (c1 - c0) * world != s.n:
-                raise SystemExit(f"{s.name}: {s.n} columns do not split evenly over {world} GPUs")
-            specs.append(dict(name=s.name, k=s.k, n=c1 - c0, n_full=s.n, rows=tokens, col=True))
-        else:
-            r0, r1 = sharding.row_shard(tokens, world, rank)
-            specs.append(dict(name=s.name, k=s.k, n=s.n, n_full=s.n, rows=r1 - r0, col=False))
-    xs = [synthetic.student_t_activations(sp["rows"], sp["k"], synthetic.linear_seed(4, p) + 1_000_003 * rank,
-                                          device=device) for p, sp in enumerate(specs)]
-    stacks, hk_w, hk_ws = [], [], []
+    specs = c4_specs(tokens, world, rank)
+    xs = c4_inputs(specs, tokens, device)
+    stacks = []
     for layer in range(layers):
-        lw = []
-        for p, sp in enumerate(specs):
-            seed = synthetic.linear_seed(4, 7 * layer + p) + 500_000 + (7919 * rank if sp["col"] else 0)
-            lw.append(synthetic.normal_fp8_weights(sp["n"], sp["k"], seed, device=device) + (None,))
-        if "codebook" in phases:
-            stacks.append(CodebookStack(lw, seed=layer))
-        if "hawkeye" in phases:
-            hk_w.append([HawkeyeOperand(w) for w, _ws, _b in lw])
-            hk_ws.append([ws.reshape(-1).to(torch.float32).contiguous() for _w, ws, _b in lw])
-        del lw
-
+        stacks.append(CodebookStack([c4_weights(sp, layer, p, device) for p, sp in enumerate(specs)], seed=layer))
+    torch.cuda.synchronize()
     mismatch = torch.zeros((1,), dtype=torch.int32, device=device)
 
     def buffer_set():
@@ -929,121 +1038,111 @@ def run_c4(args) -> None:
             b["scale"].append(torch.empty((rows,), dtype=torch.float32, device=device))
             b["code_scale"].append(torch.empty((rows,), dtype=torch.float32, device=device))
             b["planes"].append(DigitPlanes.empty(rows, k, nat.IMA_SCHEME_DIGITS3, device))
-            b["c"].append(torch.empty((rows, n), dtype=torch.int64, device=device) if "codebook" in phases else None)
+            b["c"].append(torch.empty((rows, n), dtype=torch.int64, device=device))
             b["y"].append(torch.empty((rows, n), dtype=torch.bfloat16, device=device))
         return b
 
     sets = [buffer_set(), buffer_set()]
-    views = [[dict(sets[s]) for s in range(2)] for _ in range(len(stacks))]   # own descriptor caches
-    gathered = [torch.empty((world * sp["rows"], sp["n"]), dtype=torch.bfloat16, device=device) for sp in specs]
-    hk_xop = [torch.empty((int(lib.ima_hawkeye_operand_bytes(sp["rows"], sp["k"])),), dtype=torch.uint8,
-                          device=device) for sp in specs] if "hawkeye" in phases else []
-    # the gathers get a high-priority stream, and the persistent GEMM leaves SMs to them
-    cs, ms = torch.cuda.Stream(device), torch.cuda.Stream(device, priority=-1)
-    reserve = args.c4_sm_reserve if args.c4_sm_reserve >= 0 else (16 if world > 1 and args.c4_gather == "nccl" else 0)
-    sms = torch.cuda.get_device_properties(device).multi_processor_count
-    nat.call("ima_set_gemm_sm_limit", max(sms - reserve, 1) if reserve else 0)
+    views = [[dict(sets[s]) for s in range(2)] for _ in range(layers)]   # own descriptor caches per layer
+    cs = torch.cuda.Stream(device)                    # compute
+    ms = torch.cuda.Stream(device, priority=-1)       # gather bookkeeping
+    ce_streams = [torch.cuda.Stream(device, priority=-1) for _ in range(world)]   # one per destination rank
+    ce_done = [[torch.cuda.Event() for _ in range(world)] for _ in range(2)]
     computed = [torch.cuda.Event(), torch.cuda.Event()]
     drained = [torch.cuda.Event(), torch.cuda.Event()]
 
-    # Gather of the output shards.  "ce": every rank copies its shard into every rank's
-    # gathered buffer (shared once through CUDA IPC) with peer-to-peer copies on the copy
-    # engines, which use no SM and so overlap the compute fully; "nccl": one
-    # all_gather_into_tensor per linear.
-    use_ce = world > 1 and args.c4_gather == "ce"
-    peer_bufs, own_bufs = [], []
-    if use_ce:
-        import ctypes
-
+    # Gather buffers: every rank allocates two sets of gathered outputs (one per buffer set, so
+    # that the copies of layer L and L + 1 never share a destination) and shares them through
+    # CUDA IPC; each rank copies its shard of every output into every rank's buffer.  After its
+    # copies of a buffer set a rank records an interprocess event, on which every receiver waits
+    # before the timed region ends (receiver-side completion).
+    own_bufs, peer_bufs, sent, peer_sent = [], [], [], []
+    if world > 1:
         hb = int(lib.ima_ipc_handle_bytes())
         handles = []
-        for sp in specs:
-            ptr, h = ctypes.c_void_p(), (ctypes.c_char * hb)()
-            nat.call("ima_ipc_alloc", world * sp["rows"] * sp["n"] * 2, ctypes.byref(ptr), h)
-            own_bufs.append(ptr.value)
-            handles.append(bytes(h))
-        del gathered[:]
+        for s in range(2):
+            for sp in specs:
+                ptr, h = ctypes.c_void_p(), (ctypes.c_char * hb)()
+                rows_full = tokens if not sp["col"] else tokens
+                nat.call("ima_ipc_alloc", world * sp["rows"] * sp["n"] * 2, ctypes.byref(ptr), h)
+                own_bufs.append(ptr.value)
+                handles.append(bytes(h))
+                del rows_full
+        sent = [torch.cuda.Event(interprocess=True, blocking=False) for _ in range(2)]
+        ev_handles = [e.ipc_handle() for e in sent]
         everyone = [None] * world
-        dist.all_gather_object(everyone, handles)
+        dist.all_gather_object(everyone, (handles, ev_handles))
         for q in range(world):
-            row = []
-            for p in range(len(specs)):
+            row, evs = [], []
+            for i in range(2 * len(specs)):
                 if q == rank:
-                    row.append(own_bufs[p])
+                    row.append(own_bufs[i])
                 else:
                     ptr = ctypes.c_void_p()
-                    h = (ctypes.c_char * hb).from_buffer_copy(everyone[q][p])
+                    h = (ctypes.c_char * hb).from_buffer_copy(everyone[q][0][i])
                     nat.call("ima_ipc_open", h, ctypes.byref(ptr))
                     row.append(ptr.value)
             peer_bufs.append(row)
-
-    # one copy stream per destination rank, so that several copy engines push at once
-    ce_streams = [torch.cuda.Stream(device, priority=-1) for _ in range(world)] if use_ce else []
-    ce_done = [[torch.cuda.Event() for _ in range(world)] for _ in range(2)] if use_ce else []
+            peer_sent.append([None if q == rank else torch.cuda.Event.from_ipc_handle(device, everyone[q][1][s])
+                              for s in range(2)])
 
     def gather(s: int) -> None:
+        """Copies of this rank's output shards of buffer set s into every rank's gathered
+        buffers (ordered after the GEMM that wrote them)."""
         computed[s].record(cs)
-        if world > 1:
-            if use_ce:
-                for q in range(world):
-                    st = ce_streams[(rank + q) % world]   # start at different peers on different ranks
-                    dst_rank = (rank + q) % world
-                    st.wait_event(computed[s])
-                    for p, sp in enumerate(specs):
-                        shard = sp["rows"] * sp["n"] * 2
-                        nat.call("ima_copy_async", peer_bufs[dst_rank][p] + rank * shard, sets[s]["y"][p].data_ptr(),
-                                 shard, st.cuda_stream)
-                    ce_done[s][q].record(st)
-                for q in range(world):
-                    ms.wait_event(ce_done[s][q])
-            else:
-                ms.wait_event(computed[s])
-                with torch.cuda.stream(ms):
-                    for p in range(len(specs)):
-                        dist.all_gather_into_tensor(gathered[p], sets[s]["y"][p])
-            drained[s].record(ms)
-        else:
+        if world == 1:
             drained[s].record(cs)
+            return
+        for q in range(world):
+            dst = (rank + q) % world                  # start at different peers on different ranks
+            st = ce_streams[dst]
+            st.wait_event(computed[s])
+            for p, sp in enumerate(specs):
+                shard = sp["rows"] * sp["n"] * 2
+                nat.call("ima_copy_async", peer_bufs[dst][s * len(specs) + p] + rank * shard, sets[s]["y"][p].data_ptr(),
+                         shard, st.cuda_stream)
+            ce_done[s][q].record(st)
+        for q in range(world):
+            ms.wait_event(ce_done[s][q])
+        drained[s].record(ms)
+        sent[s].record(ms)
 
-    hk_side = [torch.cuda.Stream(device) for _ in range(4)]
+    gemm_marks: list | None = None
 
-    def hawkeye_layer(layer: int, s: int) -> None:
-        sp_ = cs.cuda_stream
-        b = sets[s]
-        for p, sp in enumerate(specs):
-            rows, k = sp["rows"], sp["k"]
-            nat.check("q", lib.ima_quantize_per_token(xs[p].data_ptr(), nat.IMA_DTYPE_BF16, rows, k, k,
-                                                      b["q"][p].data_ptr(), k, b["scale"][p].data_ptr(), None, k,
-                                                      None, None, 16, sp_))
-            nat.check("p", lib.ima_hawkeye_prepare(b["q"][p].data_ptr(), rows, k, k, hk_xop[p].data_ptr(), sp_))
-        for st in hk_side:   # replays round-robin on side streams (overlapping grid tails)
-            st.wait_stream(cs)
-        for p, sp in enumerate(specs):
-            rows, k, n = sp["rows"], sp["k"], sp["n"]
-            nat.check("r", lib.ima_hawkeye_replay(hk_xop[p].data_ptr(), hk_w[layer][p].buffer.data_ptr(),
-                                                  b["scale"][p].data_ptr(), hk_ws[layer][p].data_ptr(), rows, n, k,
-                                                  32, 14, -139, b["y"][p].data_ptr(), n, None, n,
-                                                  hk_side[p % len(hk_side)].cuda_stream))
-        for st in hk_side:
-            cs.wait_stream(st)
-
-    def step(phase: str) -> None:
+    def forward_layers() -> None:
+        """One step: every layer, each on the buffer set it alternates with the previous one."""
         for layer in range(layers):
             s = layer % 2
-            if layer >= 2:
-                cs.wait_event(drained[s])   # the gather of layer - 2 has read this buffer set
+            cs.wait_event(drained[s])        # the gathers of two layers ago have read this set
+            v = views[layer][s]
             with torch.cuda.stream(cs):
-                if phase == "codebook":
-                    stacks[layer].forward(xs, views[layer][s])
-                else:
-                    hawkeye_layer(layer, s)
-            gather(s)
+                stacks[layer].quantize(xs, v)
+                if gemm_marks is not None:
+                    gemm_marks.append(torch.cuda.Event(enable_timing=True))
+                    gemm_marks[-1].record(cs)
+                stacks[layer].multiply(xs, v)
+                if gemm_marks is not None:
+                    gemm_marks.append(torch.cuda.Event(enable_timing=True))
+                    gemm_marks[-1].record(cs)
+                gather(s)
+                stacks[layer].verify(xs, v)
+
+    def finish_gathers() -> None:
+        """The end of a timed region: this rank's copies are done and every peer's copies into
+        this rank's buffers have landed."""
         for s in range(2):
             cs.wait_event(drained[s])
+        if world > 1:
+            dist.barrier()                   # every rank has enqueued its last copies and events
+            for q in range(world):
+                if q != rank:
+                    for s in range(2):
+                        cs.wait_event(peer_sent[q][s])
 
-    def timed(phase: str, steps: int, warmup: int) -> float:
+    def timed(fn, steps: int, warmup: int) -> float:
         for _ in range(warmup):
-            step(phase)
+            fn()
+        finish_gathers()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -1051,46 +1150,139 @@ def run_c4(args) -> None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(cs)
         for _ in range(steps):
-            step(phase)
+            fn()
+        finish_gathers()
         e1.record(cs)
         torch.cuda.synchronize()
-        ms_ = e0.elapsed_time(e1) / steps
-        t = torch.tensor([ms_], dtype=torch.float64, device=device)
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=device)
         if world > 1:
-            dist.barrier()
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
     shapes_full = synthetic.qwen_layer_shapes(3584, 512, 18944)
+    ops = sum(2.0 * tokens * s.n * s.k for s in shapes_full) * layers
+    local_ops = sum(2.0 * sp["rows"] * sp["n"] * sp["k"] for sp in specs) * layers
     gather_bytes = sum(2 * (world - 1) * sp["rows"] * sp["n"] for sp in specs) * layers if world > 1 else 0
-    res = {"workload": f"c4: {7 * layers} FP8 linears of Qwen2.5-7B shape ({layers} layers), {tokens} tokens "
-                       f"over {world} GPUs (token rows; gate/up output columns)",
-           "n_gpus": world, "tokens": tokens, "layers": layers, "gemm_sms_left_to_collectives": reserve,
-           "nvlink_bytes_received_per_gpu_per_step": gather_bytes,
-           "gather": ("copy engines: peer-to-peer copies into CUDA-IPC-shared buffers" if use_ce else
-                      "NCCL all_gather_into_tensor") if world > 1 else None}
+    int8_peak, peak_source = int8_tensor_peak()
+
+    # ---- timed region: device-resident inputs (2.3 GB of weight planes per layer > L2) ----
     clock = ClockSampler(local)
     clock.start()
-    if "codebook" in phases:
-        mismatch.zero_()
-        t = timed("codebook", args.c4_steps, args.c4_warmup)
-        ops = sum(2.0 * tokens * s.n * s.k for s in shapes_full) * layers
-        res["codebook"] = {"exact_tops": ops / (t * 1e-3) / 1e12, "ms_per_step": t,
-                           "exact_int_ops_per_step": ops}
-        torch.cuda.synchronize()
-        bad = mismatch.clone()
-        if world > 1:
-            dist.all_reduce(bad)
-        res["freivalds_mismatch_rows"] = int(bad.item())
-    if "hawkeye" in phases:
-        t = timed("hawkeye", max(1, args.c4_steps // 2), min(args.c4_warmup, 2))
-        outputs = sum(tokens * s.n for s in shapes_full) * layers
-        products = sum(tokens * s.n * s.k for s in shapes_full) * layers
-        res["hawkeye"] = {"outputs_per_s": outputs / (t * 1e-3), "products_per_s": products / (t * 1e-3),
-                          "ms_per_step": t}
-    res["clocks"] = clock.stop()
-    if rank == 0:
-        print(json.dumps({"c4": res}), flush=True)
+    time.sleep(0.3)
+    mismatch.zero_()
+    ms_step = timed(forward_layers, args.steps, args.warmup)
+    clocks = clock.stop()
+    bad = mismatch.clone()
+    if world > 1:
+        dist.all_reduce(bad)
+    # the GEMM's share of the step: CUDA events around each layer's GEMM launch inside one more
+    # step, so the roofline is taken inside the real step
+    gemm_marks = []
+    timed(forward_layers, 1, 0)
+    gemm_ms = sum(gemm_marks[2 * i].elapsed_time(gemm_marks[2 * i + 1]) for i in range(layers))
+    gemm_marks = None
+    gt = torch.tensor([gemm_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+    gemm_ms = float(gt.item())
+
+    # ---- end to end through the public API: host inputs in, the step's result out ----
+    host_x = [x.cpu().pin_memory() for x in xs]
+    last = len(specs) - 1                              # the final layer's down_proj
+    host_out = torch.empty(sets[(layers - 1) % 2]["y"][last].shape, dtype=torch.bfloat16).pin_memory()
+    host_bad = torch.empty((1,), dtype=torch.int32).pin_memory()
+    cin = torch.cuda.Stream(device)
+
+    def e2e_step() -> None:
+        cin.wait_stream(cs)                            # the previous step no longer reads the inputs
+        with torch.cuda.stream(cin):
+            for x, hx in zip(xs, host_x):
+                x.copy_(hx, non_blocking=True)
+        cs.wait_stream(cin)
+        forward_layers()
+        with torch.cuda.stream(cs):
+            host_out.copy_(sets[(layers - 1) % 2]["y"][last], non_blocking=True)
+            host_bad.copy_(mismatch, non_blocking=True)
+
+    e2e_ms = timed(e2e_step, max(2, min(args.steps, 5)), 1)
+    h2d = sum(x.numel() * 2 for x in xs)
+    d2h = host_out.numel() * 2 + 4
+
+    # ---- CPU baseline (rank 0 of a 1-GPU run): the reference's CPU path on sampled rows of the
+    # last two layers' linears, compared with the outputs the timed steps left in the buffers ----
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = c4_cpu_baseline(specs, stacks, xs, sets, layers, args.cpu_seconds)
+
+    fig = ncu_figure("int_gemm_kernel<DIGITS3> c4") or {}
+    gemm_tc = 9.0 * local_ops / (gemm_ms * 1e-3) / 1e12
+    line = {
+        "metric": C4_METRIC,
+        "value": round(ops / (ms_step * 1e-3) / 1e12, 3),
+        "unit": "TOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8 digit planes -> int32 TMEM -> int64",
+        "data": "synthetic (seeded Student-t activations, N(0,0.02) e4m3 weights; no checkpoint)",
+        "config": {
+            "workload": "c4: 196 FP8 linears of Qwen2.5-7B shape (28 layers), 16384 tokens in total, codebook "
+                        "student, int64 outputs + per-product Freivalds check, bf16 outputs gathered to every GPU",
+            "linears": 7 * layers,
+            "tokens": tokens,
+            "exact_int_ops_per_step": ops,
+            "parallelism": f"token rows over {world} GPU(s), gate/up output columns over {world} GPU(s)",
+            "gather": ("copy engines: peer-to-peer copies into CUDA-IPC-shared buffers, receiver-side completion by "
+                       "interprocess events" if world > 1 else None),
+            "nvlink_bytes_received_per_gpu_per_step": gather_bytes,
+            "l2": "inputs larger than L2 (2.3 GB of weight digit planes per layer)",
+            "activations": "the seven activation matrices of a layer are shared by the 28 layers (the work per "
+                           "layer is unchanged)",
+        },
+        "freivalds_mismatch_rows": int(bad.item()),
+        "gpu_launches": sum(st.launches_per_forward() for st in stacks) * args.steps,
+        "roofline": {
+            "kernel": "int_gemm_kernel<DIGITS3>",
+            "bound": "tensor",
+            "achieved": round(gemm_tc, 2),
+            "peak": round(int8_peak, 1) if int8_peak else None,
+            "unit": "TOPS (int8 tensor ops, 9 digit products per exact product)",
+            "frac": round(gemm_tc / int8_peak, 4) if int8_peak else None,
+            "peak_source": peak_source,
+            "gemm_ms_per_step": round(gemm_ms, 3),
+            "exact_tops_gemm_only": round(local_ops / (gemm_ms * 1e-3) / 1e12, 2),
+            "traffic": fig.get("dram_bytes_per_launch"),
+            "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one layer's grouped GEMM launch "
+                               f"at N = 1 ({fig.get('command')}); capture matches the current source: "
+                               f"{fig.get('current')}") if fig else None,
+            "timing": "CUDA events around each layer's GEMM launch inside one step (max over ranks)",
+        },
+        "e2e": {
+            "value": round(ops / (e2e_ms * 1e-3) / 1e12, 3),
+            "unit": "TOPS",
+            "ms_per_step": round(e2e_ms, 3),
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "api": "CodebookStack (quantize / multiply / verify per layer) with the activations copied in from "
+                   "pinned host memory each step and the step's result (the last layer's down_proj output rows "
+                   "of this GPU and the Freivalds verdict) copied back",
+        },
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "measured_peaks": {k: measured_peaks().get(k) for k in ("hbm_gbs", "bf16_tflops")},
+    }
+    del stacks, sets, views
+    torch.cuda.empty_cache()
+    # ---- config 4, Hawkeye replay phase (same partition and gathers) ----
+    if not args.no_hawkeye:
+        try:
+            line["c4_hawkeye"] = c4_hawkeye_phase(args, specs, xs, world, rank, device)
+        except Exception as exc:  # noqa: BLE001
+            line["c4_hawkeye"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     if world > 1:
         torch.cuda.synchronize()
         dist.barrier()   # every rank's copies into the shared buffers are done
@@ -1101,7 +1293,173 @@ def run_c4(args) -> None:
         dist.barrier()   # every peer has unmapped this rank's buffers
         for ptr in own_bufs:
             nat.call("ima_ipc_free", ptr)
+    if world == 1 and rank == 0:
+        for key, fn in (("c1", run_c1), ("hawkeye_c2", lambda a: run_hawkeye(a, emit=False)),
+                        ("class_counts_c3", run_class_counts_c3)):
+            if (key == "hawkeye_c2" and args.no_hawkeye) or (key == "class_counts_c3" and args.no_class_counts):
+                continue
+            try:
+                line[key] = fn(args)
+            except Exception as exc:  # noqa: BLE001
+                line[key] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.destroy_process_group()
+
+
+def c4_cpu_baseline(specs, stacks, xs, sets, layers: int, budget_s: float) -> dict:
+    """The reference's CPU path (torch quantiser expressions, torch int64 matmul, fp32 rescale)
+    on sampled token rows of the last two layers' linears, whose outputs the timed steps left in
+    the two buffer sets; rows split over all host threads.  The CPU results double as the
+    parity check of those GPU outputs (int64 products and bf16 outputs, bit for bit)."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(1)
+    rows = 64
+    done_ops, t_used, checked, ok = 0.0, 0.0, 0, True
+    try:
+        for layer in (layers - 1, layers - 2):
+            s = layer % 2
+            for p, sp in enumerate(specs):
+                if t_used >= budget_s:
+                    break
+                lin = stacks[layer].linears[p]
+                x = xs[p][:rows].cpu()
+                w, ws = lin.w_fp8.cpu(), lin.w_code_scale.cpu() * 512.0
+                bias = lin.bias.cpu() if lin.bias is not None else None
+                codes = oracle.fp8_codebook(w).to(torch.int64)
+                t0 = time.perf_counter()
+                c_ref, out_ref = oracle.torch_cpu_codebook_linear(x, w, ws.reshape(-1, 1), bias, threads=threads,
+                                                                  w_codes=codes)
+                t_used += time.perf_counter() - t0
+                done_ops += 2.0 * rows * sp["n"] * sp["k"]
+                same = torch.equal(sets[s]["c"][p][:rows].cpu(), c_ref) and torch.equal(
+                    sets[s]["y"][p][:rows].cpu().view(torch.int16), out_ref.to(torch.bfloat16).view(torch.int16))
+                ok = ok and same
+                checked += rows
+    finally:
+        torch.set_num_threads(prev)
+    return {
+        "value": round(done_ops / t_used / 1e12, 6),
+        "unit": "TOPS",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{rows} token rows of each linear of the last two layers (rows split over {threads} threads), "
+                  f"{t_used:.1f} s",
+        "parity": {"rows_checked": checked, "ok": ok,
+                   "what": "GPU int64 products and bf16 outputs of the timed steps vs the CPU results, bit for bit"},
+    }
+
+
+def c4_hawkeye_phase(args, specs, xs, world: int, rank: int, device) -> dict:
+    """Config 4 through the direct Hawkeye replay: per layer, quantise and stage the seven
+    activations, replay the seven linears (round-robin on four side streams), gather the bf16
+    outputs (NCCL all-gather per linear at N > 1).  Timed on the device, max over ranks."""
+    from int_model_approximation_b200 import _native as nat
+    from int_model_approximation_b200 import synthetic
+    from int_model_approximation_b200.hawkeye import HawkeyeOperand
+
+    dist = torch.distributed
+    lib = nat.lib()
+    tokens, layers = args.c4_tokens, args.c4_layers
+    w_ops, w_scales = [], []
+    for layer in range(layers):
+        row_ops, row_ws = [], []
+        for p, sp in enumerate(specs):
+            w, ws, _b = c4_weights(sp, layer, p, device)
+            row_ops.append(HawkeyeOperand(w))
+            row_ws.append(ws.reshape(-1).to(torch.float32).contiguous())
+            del w
+        w_ops.append(row_ops)
+        w_scales.append(row_ws)
+    q = [torch.empty((sp["rows"], sp["k"]), dtype=torch.uint8, device=device) for sp in specs]
+    scale = [torch.empty((sp["rows"],), dtype=torch.float32, device=device) for sp in specs]
+    xop = [torch.empty((int(lib.ima_hawkeye_operand_bytes(sp["rows"], sp["k"])),), dtype=torch.uint8, device=device)
+           for sp in specs]
+    ys = [[torch.empty((sp["rows"], sp["n"]), dtype=torch.bfloat16, device=device) for sp in specs] for _ in range(2)]
+    gathered = [torch.empty((world * sp["rows"], sp["n"]), dtype=torch.bfloat16, device=device) for sp in specs] \
+        if world > 1 else []
+    cs = torch.cuda.Stream(device)
+    side = [torch.cuda.Stream(device) for _ in range(4)]
+    gs = torch.cuda.Stream(device)
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def step() -> None:
+        for layer in range(layers):
+            s = layer % 2
+            cs.wait_event(done[s])
+            sp_ = cs.cuda_stream
+            for p, sp in enumerate(specs):
+                rows, k = sp["rows"], sp["k"]
+                nat.check("q", lib.ima_quantize_per_token(xs[p].data_ptr(), nat.IMA_DTYPE_BF16, rows, k, k,
+                                                          q[p].data_ptr(), k, scale[p].data_ptr(), None, k, None,
+                                                          None, 16, sp_))
+                nat.check("p", lib.ima_hawkeye_prepare(q[p].data_ptr(), rows, k, k, xop[p].data_ptr(), sp_))
+            for st in side:
+                st.wait_stream(cs)
+            for p, sp in enumerate(specs):
+                nat.check("r", lib.ima_hawkeye_replay(xop[p].data_ptr(), w_ops[layer][p].buffer.data_ptr(),
+                                                      scale[p].data_ptr(), w_scales[layer][p].data_ptr(), sp["rows"],
+                                                      sp["n"], sp["k"], 32, 14, -139, ys[s][p].data_ptr(), sp["n"],
+                                                      None, sp["n"], side[p % len(side)].cuda_stream))
+            for st in side:
+                cs.wait_stream(st)
+            if world > 1:
+                gs.wait_stream(cs)
+                with torch.cuda.stream(gs):
+                    for p in range(len(specs)):
+                        dist.all_gather_into_tensor(gathered[p], ys[s][p])
+                done[s].record(gs)
+            else:
+                done[s].record(cs)
+        for s in range(2):
+            cs.wait_event(done[s])
+
+    step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.c4_hawkeye_steps)
+    e0.record(cs)
+    for _ in range(steps):
+        step()
+    e1.record(cs)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    shapes_full = synthetic.qwen_layer_shapes(3584, 512, 18944)
+    outputs = sum(tokens * s.n for s in shapes_full) * layers
+    products = sum(tokens * s.n * s.k for s in shapes_full) * layers
+    res = {"outputs_per_s": outputs / (ms * 1e-3), "products_per_s": products / (ms * 1e-3), "ms_per_step": ms,
+           "steps": steps, "warmup": 1, "gather": "NCCL all_gather_into_tensor per linear" if world > 1 else None}
+    if world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        rows = 8
+        t_used, ok, checked = 0.0, True, 0
+        s = (layers - 1) % 2
+        for p, sp in enumerate(specs):
+            w, ws, _b = c4_weights(sp, layers - 1, p, device)
+            t0 = time.perf_counter()
+            ref = oracle.hawkeye(q[p][:rows].cpu().view(torch.float8_e4m3fn), scale[p][:rows].cpu(), w.cpu(), ws.cpu())
+            t_used += time.perf_counter() - t0
+            ok = ok and torch.equal(ys[s][p][:rows].cpu().view(torch.int16), ref.to(torch.bfloat16).view(torch.int16))
+            checked += rows
+        res["cpu_baseline"] = {
+            "value": sum(rows * sp["n"] * sp["k"] for sp in specs) / t_used, "unit": "products/s",
+            "cores": max(1, min(32, os.cpu_count() or 1)), "kind": "port",
+            "sample": f"{rows} token rows of each linear of the last layer through the oracle's C restatement of "
+                      f"the replay, {t_used:.1f} s",
+            "parity": {"rows_checked": checked, "ok": ok,
+                       "what": "GPU bf16 outputs of the timed step vs the CPU replay, bit for bit"}}
+    return res
 
 
 def main() -> None:
@@ -1114,38 +1472,39 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--hawkeye-cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-class-counts", action="store_true")
-    ap.add_argument("--reference-rows", type=int, default=TOKENS)
+    ap.add_argument("--class-counts-only", action="store_true", help="only the config-3 class-count measurement")
+    ap.add_argument("--reference-rows", type=int, default=256)
     ap.add_argument("--profile-step", action="store_true", help="two eager forwards only (for ncu)")
     ap.add_argument("--profile-tokens", type=int, default=TOKENS)
     ap.add_argument("--hawkeye-only", action="store_true", help="only the config-2 Hawkeye measurement")
     ap.add_argument("--hawkeye-tokens", type=int, default=16384)
     ap.add_argument("--hawkeye-steps", type=int, default=3)
     ap.add_argument("--no-hawkeye", action="store_true", help="skip the config-2 Hawkeye object of the default line")
-    ap.add_argument("--config4", action="store_true", help="the config-4 (7B shapes) multi-GPU measurement")
     ap.add_argument("--c4-tokens", type=int, default=16384)
     ap.add_argument("--c4-layers", type=int, default=28)
-    ap.add_argument("--c4-steps", type=int, default=4)
-    ap.add_argument("--c4-warmup", type=int, default=3)
-    ap.add_argument("--c4-phases", default="codebook,hawkeye")
-    ap.add_argument("--c4-sm-reserve", type=int, default=-1,
-                    help="SMs the GEMM leaves to the gather kernels (-1: 16 with NCCL gathers, 0 otherwise)")
-    ap.add_argument("--c4-gather", choices=["ce", "nccl"], default="ce")
+    ap.add_argument("--c4-hawkeye-steps", type=int, default=1)
+    ap.add_argument("--c1-only", action="store_true", help="only the config-1 measurement (one GPU)")
+    ap.add_argument("--profile-c4", action="store_true", help="two eager forwards of --c4-layers layers (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.config4:
-        # compute, gather, check and per-peer copy streams: more than the default 8 hardware
-        # queues, which would serialise unrelated streams (must be set before CUDA starts)
-        os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
-        run_c4(args)
+    if args.c1_only:
+        print(json.dumps({"c1": run_c1(args)}), flush=True)
     elif args.hawkeye_only:
         run_hawkeye(args)
+    elif args.class_counts_only:
+        print(json.dumps({"class_counts_c3": run_class_counts_c3(args)}), flush=True)
     elif args.profile_step:
         run_profile_step(args)
+    elif args.profile_c4:
+        run_profile_c4(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
-        run_b200(args)
+        # compute, gather bookkeeping, input and per-peer copy streams: more than the default 8
+        # hardware queues, which would serialise unrelated streams (set before CUDA starts)
+        os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+        run_headline(args)
 
 
 if __name__ == "__main__":
