@@ -302,7 +302,7 @@ def run_class_counts_c3(args) -> dict:
 
     device = torch.device("cuda", 0)
     shape = synthetic.LinearShape("down_proj", 896, 4864)
-    x, w, ws = synthetic.make_linear_inputs(3, 0, shape, device=device)
+    x, w, ws = synthetic.make_linear_inputs(3, 0, shape, tokens=args.c3_tokens, device=device)
     xq, xs, *_ = codebook.per_token_fp8(x)
     params = dict(class_chunk=512, packed_count_lanes=6, packed_group_lanes=2)
 
@@ -1473,6 +1473,7 @@ def main() -> None:
     ap.add_argument("--hawkeye-cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-class-counts", action="store_true")
     ap.add_argument("--class-counts-only", action="store_true", help="only the config-3 class-count measurement")
+    ap.add_argument("--c3-tokens", type=int, default=4096, help="token rows of config 3 (4096; fewer for ncu only)")
     ap.add_argument("--reference-rows", type=int, default=256)
     ap.add_argument("--profile-step", action="store_true", help="two eager forwards only (for ncu)")
     ap.add_argument("--profile-tokens", type=int, default=TOKENS)

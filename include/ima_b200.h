@@ -278,11 +278,14 @@ int ima_class_presence(const uint8_t* fp8, int64_t rows, int64_t K, int64_t ld, 
  * Hawkeye accumulator is replayed from the counts in the same kernel (output bit-identical to
  * ima_hawkeye_replay), and every count tile is checked with a Freivalds fingerprint before it
  * is discarded.
- * Operands are staged once each with ima_class_count_prepare into a buffer of
- * ima_class_count_operand_bytes(rows, K) bytes (16-byte aligned).
+ * Operands (activations and weights) are staged once each with ima_class_count_prepare into
+ * a buffer of ima_class_count_operand_bytes(rows, K) bytes (16-byte aligned).  A staged weight
+ * [N, K] is expanded once more with ima_class_count_weight_tiles into
+ * ima_class_count_weight_tiles_bytes(N, K) bytes: per 8 weight rows and pair of groups its
+ * one-hot slot rows, class magnitudes and the fingerprint weights, drawn from `seed`.
  * Outputs: out_bf16 and/or out_f32 [M,N] = (gfloat * x_scale[m]) * w_scale[n];
  * *mismatch_rows (device int32, zeroed by the caller) += slot rows whose count tile failed
- * the fingerprint (0 for a correct run).  `seed` draws the fingerprint weights.
+ * the fingerprint (0 for a correct run).
  * tiles_out (optional, ima_class_count_tile_entries(M, N, K) int32) receives every count tile
  * as the tensor cores formed it: tile (strip, group pair gp, tile t, group h) at index
  * ((strip * ceil(G/2) + gp) * 8 + t) * 2 + h of [128 rows][256 cols], strip = sm + sn *
@@ -292,9 +295,12 @@ int ima_class_presence(const uint8_t* fp8, int64_t rows, int64_t K, int64_t ld, 
  * same layout) replays and checks the given counts instead of the tensor-memory ones. */
 int64_t ima_class_count_operand_bytes(int64_t rows, int64_t K);
 int ima_class_count_prepare(const uint8_t* fp8, int64_t rows, int64_t K, int64_t ld, void* operand, void* stream);
+int64_t ima_class_count_weight_tiles_bytes(int64_t N, int64_t K);
+int ima_class_count_weight_tiles(const void* w_operand, int64_t N, int64_t K, uint64_t seed, void* tiles,
+                                 void* stream);
 int64_t ima_class_count_tile_entries(int64_t M, int64_t N, int64_t K);
-int ima_class_count_replay(const void* x_operand, const void* w_operand, const float* x_scale, const float* w_scale,
-                           int64_t M, int64_t N, int64_t K, uint64_t seed, uint16_t* out_bf16, int64_t ld_bf16,
+int ima_class_count_replay(const void* x_operand, const void* w_operand, const void* w_tiles, const float* x_scale,
+                           const float* w_scale, int64_t M, int64_t N, int64_t K, uint16_t* out_bf16, int64_t ld_bf16,
                            float* out_f32, int64_t ld_f32, int32_t* mismatch_rows, int32_t* tiles_out,
                            const int32_t* tiles_in, void* stream);
 

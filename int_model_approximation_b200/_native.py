@@ -97,10 +97,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ima_class_presence": (_I32, [_VP, _I64, _I64, _I64, _I64, _VP, _VP]),
     "ima_class_count_operand_bytes": (_I64, [_I64, _I64]),
     "ima_class_count_prepare": (_I32, [_VP, _I64, _I64, _I64, _VP, _VP]),
+    "ima_class_count_weight_tiles_bytes": (_I64, [_I64, _I64]),
+    "ima_class_count_weight_tiles": (_I32, [_VP, _I64, _I64, ctypes.c_uint64, _VP, _VP]),
     "ima_class_count_tile_entries": (_I64, [_I64, _I64, _I64]),
     "ima_class_count_replay": (
         _I32,
-        [_VP, _VP, _VP, _VP, _I64, _I64, _I64, ctypes.c_uint64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP],
+        [_VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP],
     ),
     "ima_planes_from_fp8": (_I32, [_VP, _I64, _I64, _I64, _VP, _I64, _VP, _VP]),
     "ima_planes_from_int32": (_I32, [_VP, _I64, _I64, _I64, _I64, _I32, _VP, _I64, _VP]),

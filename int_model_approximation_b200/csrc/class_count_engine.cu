@@ -63,48 +63,47 @@ constexpr int CE_TN = 8;                       // weight rows per MMA tile: 8 x 
 constexpr int CE_MAX_TILES = 8;                // MMA tiles per strip
 constexpr int CE_STRIP_N = CE_TN * CE_MAX_TILES;
 constexpr int CE_PITCH = 64;                   // staged rows are padded to a multiple of this
-constexpr int CE_BUILD_WARPS = 3;
+constexpr int CE_BUILD_WARPS = 2;
 constexpr int CE_EPI_WARPS = 8;
 constexpr int CE_BUILDERS = 32 * CE_BUILD_WARPS;
-constexpr int CE_THREADS = 32 * (1 + CE_BUILD_WARPS + CE_EPI_WARPS);
+constexpr int CE_FIRST_EPI_WARP = 2 + CE_BUILD_WARPS;   // warp 0 MMA, warp 1 loader, then builders
+constexpr int CE_THREADS = 32 * (CE_FIRST_EPI_WARP + CE_EPI_WARPS);
 constexpr uint32_t CE_TMEM_COLS = 512;
 constexpr int CE_ABSENT_EXP = -8192;
 constexpr uint32_t CE_NO_SLOT = 0xFFu;
 constexpr int CE_WHERE = 6;                    // where-tag of this kernel's bounded waits
+constexpr int CE_UNITS = 4;                    // unit buffers in shared memory (the loader runs ahead)
 
-// shared-memory layout (offsets from a 1024-byte aligned base)
-constexpr int CE_A_BYTES = 128 * 64;                            // 128 slot rows x 2 groups x 32 k
-constexpr int CE_B_BYTES = 256 * 64;
-constexpr int CE_OFF_A = 0;                                     // [2] buffers
-constexpr int CE_OFF_B = CE_OFF_A + 2 * CE_A_BYTES;             // [2]
-constexpr int CE_OFF_FA = CE_OFF_B + 2 * CE_B_BYTES;            // f32 [2 buf][2 h][128]
-constexpr int CE_OFF_FB = CE_OFF_FA + 2 * 2 * 128 * 4;          // f32 [2][2][256]
-constexpr int CE_OFF_RR = CE_OFF_FB + 2 * 2 * 256 * 4;          // u32 [2][2][256]
-constexpr int CE_OFF_BR = CE_OFF_RR + 2 * 2 * 256 * 4;          // s8  [2][2 h][2 half][2 vec][32 k]
-constexpr int CE_OFF_PE = CE_OFF_BR + 2 * 2 * 2 * 2 * 32;       // i32 [2][2 h][32 outputs]
-constexpr int CE_OFF_PN = CE_OFF_PE + 2 * 2 * 32 * 4;           // i32 [2][2][32]
-// staging of one unit's operand records (the 8 weight rows and the 4 tokens, both groups)
-constexpr int CE_ST_SLB = 0;                                    // u8  [2 h][8][32]
-constexpr int CE_ST_CTB = CE_ST_SLB + 2 * CE_TN * 32;           // u8  [2][8][32]
-constexpr int CE_ST_EXB = CE_ST_CTB + 2 * CE_TN * 32;           // u32 [2][8][16]
-constexpr int CE_ST_PSB = CE_ST_EXB + 2 * CE_TN * 64;           // uint4 [2][8]
-constexpr int CE_ST_SLA = CE_ST_PSB + 2 * CE_TN * 16;           // u8  [2][4][32]
-constexpr int CE_ST_CTA = CE_ST_SLA + 2 * CE_TM * 32;
-constexpr int CE_ST_EXA = CE_ST_CTA + 2 * CE_TM * 32;           // u32 [2][4][16]
-constexpr int CE_ST_PSA = CE_ST_EXA + 2 * CE_TM * 64;           // uint4 [2][4]
-constexpr int CE_STAGE_BYTES = CE_ST_PSA + 2 * CE_TM * 16;      // 3456
-constexpr int CE_OFF_STAGE = CE_OFF_PN + 2 * 2 * 32 * 4;        // [2] staging buffers
-constexpr int CE_OFF_BAR = CE_OFF_STAGE + 2 * CE_STAGE_BYTES;
-constexpr int CE_NBAR = 17;
+// Weight tile record (ima_class_count_weight_tiles), one per (8 weight rows, group pair),
+// copied into shared memory unchanged by one bulk copy:
+constexpr int CE_R_B = 0;                      // one-hot weight slot rows [256][64 B], 64-byte swizzle
+constexpr int CE_R_FB = 256 * 64;              // f32 [2 h][256]: |s| 2^e of each slot column's class
+constexpr int CE_R_RR = CE_R_FB + 2 * 256 * 4; // u32 [2][256]: fingerprint weights r1 + 2^16 r2
+constexpr int CE_R_BR = CE_R_RR + 2 * 256 * 4; // s8 [2 h][2 half][2 vec][32 k]: B^T r per half tile
+constexpr int CE_RECORD = CE_R_BR + 2 * 2 * 2 * 32;   // 20736 bytes
+// unit buffer in shared memory: the weight record, then the per-unit staging and tables
+constexpr int CE_U_EXB = CE_RECORD;                    // u32 [2 h][8][16] exponent pairs of the 8 weight rows
+constexpr int CE_U_PSB = CE_U_EXB + 2 * CE_TN * 64;    // uint4 [2][8] masks
+constexpr int CE_U_SLA = CE_U_PSB + 2 * CE_TN * 16;    // u8 [2][4][32] token slots
+constexpr int CE_U_CTA = CE_U_SLA + 2 * CE_TM * 32;    // u8 [2][4][32] token class codes
+constexpr int CE_U_EXA = CE_U_CTA + 2 * CE_TM * 32;    // u32 [2][4][16]
+constexpr int CE_U_PSA = CE_U_EXA + 2 * CE_TM * 64;    // uint4 [2][4]
+constexpr int CE_U_PE = CE_U_PSA + 2 * CE_TM * 16;     // i32 [2 h][32 outputs]: largest present exponent sum
+constexpr int CE_U_PN = CE_U_PE + 2 * 32 * 4;          // i32 [2][32]: signed present-product count
+constexpr int CE_U_END = CE_U_PN + 2 * 32 * 4;
+constexpr int CE_UNIT_BYTES = ((CE_U_END + 1023) / 1024) * 1024;   // 24576: each B tile 1024-aligned
+constexpr int CE_STAGED_BYTES = CE_U_PE - CE_RECORD;                // bytes of the per-unit bulk copies
+constexpr int CE_A_BYTES = 128 * 64;                   // one-hot token slot rows, both groups
+constexpr int CE_OFF_U = 0;
+constexpr int CE_OFF_A = CE_OFF_U + CE_UNITS * CE_UNIT_BYTES;      // [2]
+constexpr int CE_OFF_FA = CE_OFF_A + 2 * CE_A_BYTES;               // f32 [2 buf][2 h][128]
+constexpr int CE_OFF_BAR = CE_OFF_FA + 2 * 2 * 128 * 4;
+// barriers: s_full[U], b_full[U], b_empty[U], a_full[2], a_empty[2], t_full[2], t_empty[2], drained
+constexpr int CE_NBAR = 3 * CE_UNITS + 9;
 constexpr int CE_TOTAL = CE_OFF_BAR + CE_NBAR * 8 + 16;
 constexpr int CE_ALLOC = CE_TOTAL + 1024;
+static_assert(CE_RECORD % 16 == 0 && CE_U_EXB % 16 == 0 && CE_U_PSA % 16 == 0, "bulk copies need 16-byte alignment");
 
-// Staged operand (ima_class_count_prepare), per group g and row r, pitch P rows:
-//   SL [G][P][32] u8    slot of k's class among the row's classes in the group (0xFF: zero element)
-//   CT [G][P][32] u8    e4m3 code of slot s's class (0 for unused slots)
-//   EX [G][P][16] u32   int16 pairs: effective exponent of k = 2j, 2j+1 (-8192 for a zero element)
-//   PS [G][P]     uint4 {bit k: k has a class, bit k: its sign, bit s: slot s's class is negative,
-//                        number of slots used}
 struct CeOperand {
     uint8_t* sl;
     uint8_t* ct;
@@ -198,9 +197,62 @@ IMA_DEVINL uint4 ce_onehot_chunk(uint4 slots, uint32_t s, uint32_t one) {
 // Byte offset of (row, 16-byte chunk c) in a K-major tile of 64-byte rows with the 64-byte
 // swizzle (the layout a TMA SWIZZLE_64B load writes and umma_desc_sw64_kmajor describes).
 IMA_DEVINL uint32_t ce_sw64(uint32_t row, uint32_t c) { return row * 64u + ((c ^ ((row >> 1) & 3u)) << 4); }
+// Weight tile records: for each 8 weight rows `nt` and group pair `gp`, the one-hot weight
+// slot rows (carrying the class sign) in the layout the MMA reads, the slot columns' class
+// magnitudes, the fingerprint weights and B^T r.  They depend on the weight alone, so they
+// are built once per weight (one block per record).
+__global__ void __launch_bounds__(256) ce_weight_tiles_kernel(CeOperand B, int64_t GP, uint64_t seed,
+                                                            unsigned char* __restrict__ out) {
+    const int64_t nt = blockIdx.x, gp = blockIdx.y;
+    unsigned char* rec = out + (nt * GP + gp) * (int64_t)CE_RECORD;
+    const int64_t n0 = nt * CE_TN, G = B.groups;
+    for (int i = threadIdx.x; i < 256 * 4; i += blockDim.x) {
+        const uint32_t row = (uint32_t)(i >> 2), c = (uint32_t)(i & 3);
+        const uint32_t h = c >> 1, nl = row >> 5, s = row & 31u;
+        const int64_t g = 2 * gp + h;
+        uint4 sl = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+        uint32_t one = 1u;
+        if (g < G) {
+            const int64_t r = g * B.pitch + n0 + nl;
+            sl = *reinterpret_cast<const uint4*>(B.sl + r * 32 + (c & 1u) * 16);
+            one = ((B.ps[r].z >> s) & 1u) ? 0xFFu : 1u;
+        }
+        *reinterpret_cast<uint4*>(rec + CE_R_B + ce_sw64(row, c)) = ce_onehot_chunk(sl, s, one);
+    }
+    float* FB = reinterpret_cast<float*>(rec + CE_R_FB);
+    uint32_t* RR = reinterpret_cast<uint32_t*>(rec + CE_R_RR);
+    const uint64_t tile = (uint64_t)(nt * GP + gp);
+    for (int i = threadIdx.x; i < 2 * 256; i += blockDim.x) {
+        const int h = i >> 8, col = i & 255;
+        const int64_t g = 2 * gp + h;
+        const uint32_t code = g < G ? B.ct[(g * B.pitch + n0 + (col >> 5)) * 32 + (col & 31)] : 0u;
+        FB[i] = ce_magnitude(code);
+        RR[i] = ce_fingerprint_weight(seed, tile * 2 + h, (uint32_t)col);
+    }
+    int8_t* BR = reinterpret_cast<int8_t*>(rec + CE_R_BR);
+    for (int i = threadIdx.x; i < 2 * 2 * 32; i += blockDim.x) {
+        const int h = i >> 6, half = (i >> 5) & 1, k = i & 31;
+        const int64_t g = 2 * gp + h;
+        int s1 = 0, s2 = 0;
+        if (g < G) {
+            for (int nl = half * 4; nl < half * 4 + 4; ++nl) {
+                const int64_t r = g * B.pitch + n0 + nl;
+                const uint32_t slot = B.sl[r * 32 + k];
+                if (slot == CE_NO_SLOT) continue;
+                const uint32_t rr = ce_fingerprint_weight(seed, tile * 2 + h, (uint32_t)(nl * 32 + slot));
+                const bool neg = (B.ps[r].z >> slot) & 1u;
+                s1 += neg ? -(int)(rr & 0xFFFFu) : (int)(rr & 0xFFFFu);
+                s2 += neg ? -(int)(rr >> 16) : (int)(rr >> 16);
+            }
+        }
+        BR[((h * 2 + half) * 2 + 0) * 32 + k] = (int8_t)s1;
+        BR[((h * 2 + half) * 2 + 1) * 32 + k] = (int8_t)s2;
+    }
+}
 
 struct CeParams {
     CeOperand a, b;
+    const unsigned char* w_tiles;
     const float* xs;
     const float* ws;
     int64_t M, N, groups, strips_m, strips_n;
@@ -211,12 +263,10 @@ struct CeParams {
     int32_t* mismatch;
     int32_t* tiles_out;
     const int32_t* tiles_in;
-    uint64_t seed;
 };
 
-// As mbar_wait_or_abort, but each try_wait may suspend the thread (up to 20 us, or until the
-// phase completes) instead of spinning, so waiting warps leave their issue slots to the warps
-// that work.
+// mbarrier try_wait that may suspend the thread (up to 20 us, or until the phase completes)
+// instead of spinning, so waiting warps leave their issue slots to the warps that work.
 IMA_DEVINL bool ce_try_wait_sleep(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -229,6 +279,7 @@ IMA_DEVINL bool ce_try_wait_sleep(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Bounded, abort-aware wait (as mbar_wait_or_abort) built on the suspending try_wait.
 IMA_DEVINL bool ce_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns, int detail) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = ima_globaltimer();
@@ -282,25 +333,51 @@ IMA_DEVINL void ce_bulk_copy(void* smem_dst, const void* gsrc, uint32_t bytes, u
                  : "memory");
 }
 
-// Stage the operand records of the unit at `c` into one staging buffer: for both groups of the
-// pair, the 8 weight rows' and the 4 tokens' slots, codes, exponent pairs and masks (16 copies
-// of 64 to 512 bytes, all 16-byte aligned).
-IMA_DEVINL void ce_stage_unit(const CeParams& P, const CeCursor& c, unsigned char* dst, uint64_t* bar) {
+// Stage the unit at `c` into a unit buffer: the weight tile record, and for both groups of the
+// pair the 8 weight rows' exponent pairs and masks and the 4 tokens' slots, codes, exponent
+// pairs and masks (all 16-byte aligned).
+IMA_DEVINL void ce_stage_unit(const CeParams& P, const CeCursor& c, int64_t GP, unsigned char* dst, uint64_t* bar) {
     const int64_t m0 = (c.sid % P.strips_m) * CE_TM;
-    const int64_t nt = (c.sid / P.strips_m) * CE_STRIP_N + (int64_t)c.t * CE_TN;
+    const int64_t ntile = (c.sid / P.strips_m) * CE_MAX_TILES + c.t;
+    const int64_t nt = ntile * CE_TN;
     const int live = (2 * c.gp + 1 < P.groups) ? 2 : 1;
-    mbar_arrive_expect_tx(bar, (uint32_t)(live * (CE_TN + CE_TM) * (32 + 32 + 64 + 16)));
+    mbar_arrive_expect_tx(bar, (uint32_t)(CE_RECORD + live * (CE_STAGED_BYTES / 2)));
+    ce_bulk_copy(dst, P.w_tiles + (ntile * GP + c.gp) * (int64_t)CE_RECORD, CE_RECORD, bar);
     for (int h = 0; h < live; ++h) {
         const int64_t g = 2 * c.gp + h;
         const int64_t rb = g * P.b.pitch + nt, ra = g * P.a.pitch + m0;
-        ce_bulk_copy(dst + CE_ST_SLB + h * CE_TN * 32, P.b.sl + rb * 32, CE_TN * 32, bar);
-        ce_bulk_copy(dst + CE_ST_CTB + h * CE_TN * 32, P.b.ct + rb * 32, CE_TN * 32, bar);
-        ce_bulk_copy(dst + CE_ST_EXB + h * CE_TN * 64, P.b.ex + rb * 16, CE_TN * 64, bar);
-        ce_bulk_copy(dst + CE_ST_PSB + h * CE_TN * 16, P.b.ps + rb, CE_TN * 16, bar);
-        ce_bulk_copy(dst + CE_ST_SLA + h * CE_TM * 32, P.a.sl + ra * 32, CE_TM * 32, bar);
-        ce_bulk_copy(dst + CE_ST_CTA + h * CE_TM * 32, P.a.ct + ra * 32, CE_TM * 32, bar);
-        ce_bulk_copy(dst + CE_ST_EXA + h * CE_TM * 64, P.a.ex + ra * 16, CE_TM * 64, bar);
-        ce_bulk_copy(dst + CE_ST_PSA + h * CE_TM * 16, P.a.ps + ra, CE_TM * 16, bar);
+        ce_bulk_copy(dst + CE_U_EXB + h * CE_TN * 64, P.b.ex + rb * 16, CE_TN * 64, bar);
+        ce_bulk_copy(dst + CE_U_PSB + h * CE_TN * 16, P.b.ps + rb, CE_TN * 16, bar);
+        ce_bulk_copy(dst + CE_U_SLA + h * CE_TM * 32, P.a.sl + ra * 32, CE_TM * 32, bar);
+        ce_bulk_copy(dst + CE_U_CTA + h * CE_TM * 32, P.a.ct + ra * 32, CE_TM * 32, bar);
+        ce_bulk_copy(dst + CE_U_EXA + h * CE_TM * 64, P.a.ex + ra * 16, CE_TM * 64, bar);
+        ce_bulk_copy(dst + CE_U_PSA + h * CE_TM * 16, P.a.ps + ra, CE_TM * 16, bar);
+    }
+}
+static_assert(CE_STAGED_BYTES == 2 * (CE_TN * 64 + CE_TN * 16 + CE_TM * 32 * 2 + CE_TM * 64 + CE_TM * 16),
+              "the per-unit copies fill the staging area exactly");
+
+// tcgen05.wait::ld that also names the 16 registers the last tcgen05.ld wrote, so that the
+// compiler cannot schedule a use of them before the wait.
+IMA_DEVINL void ce_wait_ld(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+// 16 supplied counts of one tile row (tiles_in layout, include/ima_b200.h).
+IMA_DEVINL void ce_load_supplied(const int32_t* tiles, int64_t tile_id, int row, int col0, uint32_t (&c)[16]) {
+    const int4* src = reinterpret_cast<const int4*>(tiles + (tile_id * 128 + row) * 256 + col0);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        const int4 x = src[v];
+        c[4 * v] = (uint32_t)x.x;
+        c[4 * v + 1] = (uint32_t)x.y;
+        c[4 * v + 2] = (uint32_t)x.z;
+        c[4 * v + 3] = (uint32_t)x.w;
     }
 }
 
@@ -315,13 +392,14 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
     // access below stays a shared-memory access (not a generic one)
     unsigned char* smem = ce_raw + ((1024u - (smem_u32(ce_raw) & 1023u)) & 1023u);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CE_OFF_BAR);
-    uint64_t* a_full = bars;           // [2] builders -> MMA, epilogue
-    uint64_t* a_empty = bars + 2;      // [2] MMA commit + epilogue warps -> builders
-    uint64_t* b_full = bars + 4;       // [2]
-    uint64_t* b_empty = bars + 6;      // [2]
-    uint64_t* t_full = bars + 8;       // [2] MMA commit -> epilogue
-    uint64_t* t_empty = bars + 10;     // [2] epilogue warps -> MMA
-    uint64_t* drained = bars + 12;       // bars 13-16: the builders' staging barriers
+    uint64_t* s_full = bars;                        // [U] loader's copies landed (expect_tx)
+    uint64_t* b_full = bars + CE_UNITS;             // [U] builders' per-unit tables ready
+    uint64_t* b_empty = bars + 2 * CE_UNITS;        // [U] MMA commit + epilogue warps: unit buffer free
+    uint64_t* a_full = bars + 3 * CE_UNITS;         // [2] one-hot token rows built
+    uint64_t* a_empty = a_full + 2;                 // [2] MMA commit + epilogue warps
+    uint64_t* t_full = a_full + 4;                  // [2] count tile in tensor memory
+    uint64_t* t_empty = a_full + 6;                 // [2] epilogue warps read it
+    uint64_t* drained = a_full + 8;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + CE_NBAR);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -331,19 +409,18 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
     const int64_t strips = P.strips_m * P.strips_n;
 
     if (threadIdx.x == 0) {
+        for (int i = 0; i < CE_UNITS; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&b_full[i], CE_BUILDERS);
+            mbar_init(&b_empty[i], 1 + CE_EPI_WARPS);
+        }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&a_full[i], CE_BUILDERS);
             mbar_init(&a_empty[i], 1 + CE_EPI_WARPS);
-            mbar_init(&b_full[i], CE_BUILDERS);
-            mbar_init(&b_empty[i], 1 + CE_EPI_WARPS);
             mbar_init(&t_full[i], 1);
             mbar_init(&t_empty[i], CE_EPI_WARPS);
         }
         mbar_init(drained, 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&bars[13 + i], 1);              // staging copies: one expect_tx arrival
-            mbar_init(&bars[15 + i], CE_BUILDERS);
-        }
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -360,31 +437,30 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
             constexpr uint32_t idesc = idesc_i8(128, 256);
-            uint64_t a_cnt = 0, u_cnt = 0;
+            uint64_t a_cnt = 0, u = 0;
             bool ok = true;
             for (int64_t sid = blockIdx.x; sid < strips && ok; sid += gridDim.x) {
-                const int64_t n0 = (sid / P.strips_m) * CE_STRIP_N;
-                const int tiles = (int)min((int64_t)CE_MAX_TILES, (P.N - n0 + CE_TN - 1) / CE_TN);
+                const int tiles = ce_strip_tiles(P, sid);
                 for (int64_t gp = 0; gp < GP && ok; ++gp) {
-                    const uint32_t abuf = a_cnt & 1u, aph = (a_cnt >> 1) & 1u;
+                    const uint32_t abuf = (uint32_t)(a_cnt & 1u), aph = (uint32_t)((a_cnt >> 1) & 1u);
                     ++a_cnt;
                     ok = ce_wait(&a_full[abuf], aph, abort_flag, LIMIT, 1);
                     for (int t = 0; t < tiles && ok; ++t) {
-                        // B buffers alternate between units; each TMEM tile h is used once per unit
-                        const uint32_t ubuf = u_cnt & 1u, uph = (u_cnt >> 1) & 1u, tph = u_cnt & 1u;
-                        ++u_cnt;
-                        ok = ce_wait(&b_full[ubuf], uph, abort_flag, LIMIT, 2);
+                        const uint32_t slot = (uint32_t)(u % CE_UNITS), sph = (uint32_t)((u / CE_UNITS) & 1u);
+                        const uint32_t tph = (uint32_t)(u & 1u);   // each tensor-memory tile is used once per unit
+                        ++u;
+                        ok = ce_wait(&s_full[slot], sph, abort_flag, LIMIT, 2);
                         for (int h = 0; h < 2 && ok; ++h) {
                             ok = ce_wait(&t_empty[h], tph ^ 1u, abort_flag, LIMIT, 3);
                             if (!ok) break;
                             tc_fence_after();
                             const uint32_t sa = smem_u32(smem + CE_OFF_A + abuf * CE_A_BYTES) + h * 32;
-                            const uint32_t sb = smem_u32(smem + CE_OFF_B + ubuf * CE_B_BYTES) + h * 32;
+                            const uint32_t sb = smem_u32(smem + CE_OFF_U + slot * CE_UNIT_BYTES + CE_R_B) + h * 32;
                             mma_i8(tmem_base + (uint32_t)(h * 256), umma_desc_sw64_kmajor(sa), umma_desc_sw64_kmajor(sb),
                                    idesc, 0u);
                             mma_commit(&t_full[h]);
                         }
-                        if (ok) mma_commit(&b_empty[ubuf]);
+                        if (ok) mma_commit(&b_empty[slot]);
                     }
                     if (ok) mma_commit(&a_empty[abuf]);
                 }
@@ -393,59 +469,49 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
             mma_commit(drained);
             mbar_wait_bounded(drained, 0u, CE_WHERE, 9);
         }
-    } else if (warp <= CE_BUILD_WARPS) {
-        // ---------------- operand builders ----------------
-        // Builder thread 0 also stages each unit's operand records (the 8 weight rows and the 4
-        // tokens of both groups: slots, codes, exponent pairs, masks) into shared memory with
-        // bulk asynchronous copies, one unit ahead; the builders then work from shared memory.
-        const int tb = threadIdx.x - 32;
-        const bool loader = tb == 0;
-        float* FA = reinterpret_cast<float*>(smem + CE_OFF_FA);
-        float* FB = reinterpret_cast<float*>(smem + CE_OFF_FB);
-        uint32_t* RR = reinterpret_cast<uint32_t*>(smem + CE_OFF_RR);
-        int8_t* BR = reinterpret_cast<int8_t*>(smem + CE_OFF_BR);
-        int32_t* PE = reinterpret_cast<int32_t*>(smem + CE_OFF_PE);
-        int32_t* PN = reinterpret_cast<int32_t*>(smem + CE_OFF_PN);
-        uint64_t* s_full = bars + 13;    // [2] staging copies landed (expect_tx)
-        uint64_t* s_empty = bars + 15;   // [2] builders done with a staging buffer
-        CeCursor cur = ce_cursor_first(P, strips), nxt = cur;
-        uint64_t u = 0, a_cnt = 0, issued = 0;
-        bool ok = true;
-        if (loader && nxt.valid) {
-            ce_stage_unit(P, nxt, smem + CE_OFF_STAGE, &s_full[0]);
-            ++issued;
-            ce_cursor_next(nxt, P, strips, GP);
-        }
-        while (cur.valid && ok) {
-            const uint32_t sbuf = (uint32_t)(u & 1u), sph = (uint32_t)((u >> 1) & 1u);
-            if (loader && nxt.valid) {
-                // unit u + 1 goes into the other buffer, last read by unit u - 1
-                const uint64_t v = u + 1;
-                ok = ce_wait(&s_empty[v & 1u], (uint32_t)(((v >> 1) & 1u) ^ 1u), abort_flag, LIMIT, 10);
-                if (ok) {
-                    ce_stage_unit(P, nxt, smem + CE_OFF_STAGE + (v & 1u) * CE_STAGE_BYTES, &s_full[v & 1u]);
-                    ++issued;
-                    ce_cursor_next(nxt, P, strips, GP);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- loader: bulk copies of each unit's operands, up to CE_UNITS ahead ----
+            CeCursor c = ce_cursor_first(P, strips);
+            uint64_t v = 0;
+            bool ok = true;
+            while (c.valid && ok) {
+                const uint32_t slot = (uint32_t)(v % CE_UNITS), ph = (uint32_t)((v / CE_UNITS) & 1u);
+                ok = ce_wait(&b_empty[slot], ph ^ 1u, abort_flag, LIMIT, 10);
+                if (!ok) break;
+                ce_stage_unit(P, c, GP, smem + CE_OFF_U + slot * CE_UNIT_BYTES, &s_full[slot]);
+                ++v;
+                ce_cursor_next(c, P, strips, GP);
+            }
+            // every bulk copy issued has landed before the CTA can exit
+            for (uint64_t s = 0; s < CE_UNITS; ++s) {
+                if (v > s) {
+                    const uint64_t last = v - 1 - ((v - 1 - s) % CE_UNITS);   // last unit staged into slot s
+                    mbar_wait_bounded(&s_full[s], (uint32_t)((last / CE_UNITS) & 1u), CE_WHERE, 12);
                 }
             }
-            ok = ok && ce_wait(&s_full[sbuf], sph, abort_flag, LIMIT, 11);
+            if (!ok) *abort_flag = 1;
+        }
+    } else if (warp < CE_FIRST_EPI_WARP) {
+        // ---------------- builders: one-hot token rows per group pair, per-output tables ----
+        const int tb = threadIdx.x - 64;
+        float* FA = reinterpret_cast<float*>(smem + CE_OFF_FA);
+        CeCursor c = ce_cursor_first(P, strips);
+        uint64_t u = 0, a_cnt = 0;
+        bool ok = true;
+        while (c.valid && ok) {
+            const uint32_t slot = (uint32_t)(u % CE_UNITS), sph = (uint32_t)((u / CE_UNITS) & 1u);
+            ok = ce_wait(&s_full[slot], sph, abort_flag, LIMIT, 11);
             if (!ok) break;
-            const unsigned char* S = smem + CE_OFF_STAGE + sbuf * CE_STAGE_BYTES;
-            const uint8_t* SLB = S + CE_ST_SLB;
-            const uint8_t* CTB = S + CE_ST_CTB;
-            const uint32_t* EXB = reinterpret_cast<const uint32_t*>(S + CE_ST_EXB);
-            const uint4* PSB = reinterpret_cast<const uint4*>(S + CE_ST_PSB);
-            const uint8_t* SLA = S + CE_ST_SLA;
-            const uint8_t* CTA = S + CE_ST_CTA;
-            const uint32_t* EXA = reinterpret_cast<const uint32_t*>(S + CE_ST_EXA);
-            const uint4* PSA = reinterpret_cast<const uint4*>(S + CE_ST_PSA);
-            const int64_t gp = cur.gp;
-            if (cur.t == 0) {
-                // A of the group pair: token classes of both groups
+            unsigned char* U = smem + CE_OFF_U + slot * CE_UNIT_BYTES;
+            const int64_t gp = c.gp;
+            if (c.t == 0) {
                 const uint32_t abuf = (uint32_t)(a_cnt & 1u), aph = (uint32_t)((a_cnt >> 1) & 1u);
                 ++a_cnt;
                 ok = ce_wait(&a_empty[abuf], aph ^ 1u, abort_flag, LIMIT, 4);
                 if (!ok) break;
+                const uint8_t* SLA = U + CE_U_SLA;
+                const uint8_t* CTA = U + CE_U_CTA;
                 unsigned char* As = smem + CE_OFF_A + abuf * CE_A_BYTES;
                 for (int i = tb; i < 2 * 128; i += CE_BUILDERS) {
                     const int h = i >> 7, row = i & 127;
@@ -454,40 +520,23 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                     FA[(abuf * 2 + h) * 128 + row] = (code & 0x80u) ? -mag : mag;
                 }
                 for (int i = tb; i < 128 * 4; i += CE_BUILDERS) {
-                    const uint32_t row = (uint32_t)(i >> 2), c = (uint32_t)(i & 3);   // 8 rows x 4 chunks per warp store
-                    const uint32_t h = c >> 1;
+                    const uint32_t row = (uint32_t)(i >> 2), cc = (uint32_t)(i & 3);   // 8 rows x 4 chunks per warp store
+                    const uint32_t h = cc >> 1;
                     uint4 sl = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
                     if (2 * gp + h < G)
-                        sl = *reinterpret_cast<const uint4*>(SLA + (h * CE_TM + (row >> 5)) * 32 + (c & 1u) * 16);
-                    *reinterpret_cast<uint4*>(As + ce_sw64(row, c)) = ce_onehot_chunk(sl, row & 31u, 1u);
+                        sl = *reinterpret_cast<const uint4*>(SLA + (h * CE_TM + (row >> 5)) * 32 + (cc & 1u) * 16);
+                    *reinterpret_cast<uint4*>(As + ce_sw64(row, cc)) = ce_onehot_chunk(sl, row & 31u, 1u);
                 }
                 fence_proxy_async_smem();
                 mbar_arrive(&a_full[abuf]);
             }
-            const uint32_t ubuf = (uint32_t)(u & 1u), uph = (uint32_t)((u >> 1) & 1u);
-            ok = ce_wait(&b_empty[ubuf], uph ^ 1u, abort_flag, LIMIT, 5);
-            if (!ok) break;
-            unsigned char* Bs = smem + CE_OFF_B + ubuf * CE_B_BYTES;
-            // one-hot weight slot rows carrying the class sign
-            for (int i = tb; i < 256 * 4; i += CE_BUILDERS) {
-                const uint32_t row = (uint32_t)(i >> 2), c = (uint32_t)(i & 3);
-                const uint32_t h = c >> 1, nl = row >> 5, sl_i = row & 31u;
-                uint4 sl = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-                uint32_t one = 1u;
-                if (2 * gp + h < G) {
-                    sl = *reinterpret_cast<const uint4*>(SLB + (h * CE_TN + nl) * 32 + (c & 1u) * 16);
-                    one = ((PSB[h * CE_TN + nl].z >> sl_i) & 1u) ? 0xFFu : 1u;
-                }
-                *reinterpret_cast<uint4*>(Bs + ce_sw64(row, c)) = ce_onehot_chunk(sl, sl_i, one);
-            }
-            // class magnitudes and fingerprint weights of the 256 slot columns, both groups
-            for (int i = tb; i < 2 * 256; i += CE_BUILDERS) {
-                const int h = i >> 8, col = i & 255;
-                const uint32_t code = 2 * gp + h < G ? CTB[(h * CE_TN + (col >> 5)) * 32 + (col & 31)] : 0u;
-                FB[(ubuf * 2 + h) * 256 + col] = ce_magnitude(code);
-                RR[(ubuf * 2 + h) * 256 + col] = ce_fingerprint_weight(P.seed, u * 2 + h, (uint32_t)col);
-            }
             // each output's largest present exponent sum and signed present count
+            const uint32_t* EXA = reinterpret_cast<const uint32_t*>(U + CE_U_EXA);
+            const uint32_t* EXB = reinterpret_cast<const uint32_t*>(U + CE_U_EXB);
+            const uint4* PSA = reinterpret_cast<const uint4*>(U + CE_U_PSA);
+            const uint4* PSB = reinterpret_cast<const uint4*>(U + CE_U_PSB);
+            int32_t* PE = reinterpret_cast<int32_t*>(U + CE_U_PE);
+            int32_t* PN = reinterpret_cast<int32_t*>(U + CE_U_PN);
             for (int i = tb; i < 2 * 32; i += CE_BUILDERS) {
                 const int h = i >> 5, o = i & 31, ml = o >> 3, nl = o & 7;
                 int pe = -16384, pn = 0;
@@ -502,57 +551,20 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                     const uint32_t both = pa.x & pb.x;
                     pn = __popc(both) - 2 * __popc(both & (pa.y ^ pb.y));
                 }
-                PE[(ubuf * 2 + h) * 32 + o] = pe;
-                PN[(ubuf * 2 + h) * 32 + o] = pn;
+                PE[i] = pe;
+                PN[i] = pn;
             }
-            // B^T r per k: the weight side of the fingerprint, two int8 vectors for each half of
-            // the tile's weight rows (an epilogue warp sees the columns of one half); the weights
-            // are recomputed from their hash rather than read back from RR, so the builders need
-            // no barrier among themselves
-            for (int i = tb; i < 2 * 2 * 32; i += CE_BUILDERS) {
-                const int h = i >> 6, half = (i >> 5) & 1, k = i & 31;
-                int s1 = 0, s2 = 0;
-                if (2 * gp + h < G) {
-#pragma unroll
-                    for (int nl = half * 4; nl < half * 4 + 4; ++nl) {
-                        const uint32_t slot = SLB[(h * CE_TN + nl) * 32 + k];
-                        if (slot == CE_NO_SLOT) continue;
-                        const uint32_t rr = ce_fingerprint_weight(P.seed, u * 2 + h, (uint32_t)(nl * 32 + slot));
-                        const bool neg = (PSB[h * CE_TN + nl].z >> slot) & 1u;
-                        s1 += neg ? -(int)(rr & 0xFFFFu) : (int)(rr & 0xFFFFu);
-                        s2 += neg ? -(int)(rr >> 16) : (int)(rr >> 16);
-                    }
-                }
-                BR[(((ubuf * 2 + h) * 2 + half) * 2 + 0) * 32 + k] = (int8_t)s1;
-                BR[(((ubuf * 2 + h) * 2 + half) * 2 + 1) * 32 + k] = (int8_t)s2;
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(&b_full[ubuf]);
-            mbar_arrive(&s_empty[sbuf]);
+            mbar_arrive(&b_full[slot]);
             ++u;
-            ce_cursor_next(cur, P, strips, GP);
-        }
-        if (loader) {
-            // drain: every staging copy issued has landed before the CTA can exit
-            for (uint64_t b = 0; b < 2; ++b) {
-                if (issued > b) {
-                    const uint64_t last = issued - 1 - ((issued - 1 - b) & 1u);   // last unit staged into buffer b
-                    mbar_wait_bounded(&s_full[b], (uint32_t)((last >> 1) & 1u), CE_WHERE, 12);
-                }
-            }
+            ce_cursor_next(c, P, strips, GP);
         }
         if (!ok) *abort_flag = 1;
     } else {
         // ---------------- epilogue: replay from the counts ----------------
         const int q = warp & 3;                      // token of the strip = TMEM lane quadrant
-        const int hn = (warp - 1 - CE_BUILD_WARPS) >> 2;   // which 4 of a tile's 8 weight rows
+        const int hn = (warp - CE_FIRST_EPI_WARP) >> 2;   // which 4 of a tile's 8 weight rows
         const unsigned FULL = 0xFFFFFFFFu;
         const float* FA = reinterpret_cast<const float*>(smem + CE_OFF_FA);
-        const float* FB = reinterpret_cast<const float*>(smem + CE_OFF_FB);
-        const uint32_t* RR = reinterpret_cast<const uint32_t*>(smem + CE_OFF_RR);
-        const int8_t* BR = reinterpret_cast<const int8_t*>(smem + CE_OFF_BR);
-        const int32_t* PE = reinterpret_cast<const int32_t*>(smem + CE_OFF_PE);
-        const int32_t* PN = reinterpret_cast<const int32_t*>(smem + CE_OFF_PN);
         const int row = q * 32 + lane;               // this thread's slot row of the MMA tile
         uint64_t a_cnt = 0, u_cnt = 0;
         bool ok = true;
@@ -567,10 +579,13 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                 ok = ce_wait(&a_full[abuf], aph, abort_flag, LIMIT, 6);
                 if (!__all_sync(FULL, ok)) { ok = false; break; }
                 for (int t = 0; t < tiles && ok; ++t) {
-                    const uint32_t ubuf = u_cnt & 1u, uph = (u_cnt >> 1) & 1u, tph = u_cnt & 1u;
+                    const uint32_t slot = (uint32_t)(u_cnt % CE_UNITS), sph = (uint32_t)((u_cnt / CE_UNITS) & 1u);
+                    const uint32_t tph = (uint32_t)(u_cnt & 1u);
                     ++u_cnt;
-                    ok = ce_wait(&b_full[ubuf], uph, abort_flag, LIMIT, 7);
+                    ok = ce_wait(&b_full[slot], sph, abort_flag, LIMIT, 7);
+                    ok = ok && ce_wait(&s_full[slot], sph, abort_flag, LIMIT, 7);   // the record's bytes are visible
                     if (!__all_sync(FULL, ok)) { ok = false; break; }
+                    const unsigned char* U = smem + CE_OFF_U + slot * CE_UNIT_BYTES;
                     for (int h = 0; h < 2; ++h) {
                         const int64_t g = 2 * gp + h;
                         ok = ce_wait(&t_full[h], tph, abort_flag, LIMIT, 8);
@@ -580,8 +595,12 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                         // M_S of this warp's four outputs of the tile (owner lanes 4t .. 4t + 3)
                         const int own_i = lane & 3;
                         const int own_o = q * 8 + 4 * hn + own_i;
-                        const int tb = (int)(ubuf * 2 + h);
-                        const int pe = PE[tb * 32 + own_o];
+                        const float* FB = reinterpret_cast<const float*>(U + CE_R_FB) + h * 256;
+                        const uint32_t* RR = reinterpret_cast<const uint32_t*>(U + CE_R_RR) + h * 256;
+                        const int8_t* BR = reinterpret_cast<const int8_t*>(U + CE_R_BR) + h * 128;
+                        const int32_t* PE = reinterpret_cast<const int32_t*>(U + CE_U_PE) + h * 32;
+                        const int32_t* PN = reinterpret_cast<const int32_t*>(U + CE_U_PN) + h * 32;
+                        const int pe = PE[own_o];
                         const int acc_e14 = (int)((__float_as_uint(acc) << 1) >> 24) - 133;
                         const uint32_t ms_own = (uint32_t)max(pe, acc_e14) * (1u << 23) + ((143u << 23) | 0x400000u);
                         uint32_t ms[4];
@@ -589,51 +608,56 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                         for (int i = 0; i < 4; ++i) ms[i] = __shfl_sync(FULL, ms_own, t * 4 + i);
                         const float fa = FA[(abuf * 2 + h) * 128 + row];
                         const float fa_abs = fabsf(fa);
-                        uint32_t part[4], fp = 0;
+                        uint32_t part[4] = {0u, 0u, 0u, 0u}, fp = 0;
                         const int64_t tile_id = (((sid * GP + gp) * CE_MAX_TILES + t) * 2 + h);
+                        // 8 chunks of 16 count columns (weight row 4 hn + (chunk >> 1), slots
+                        // 16 (chunk & 1) ..): the tensor-memory load of chunk j + 1 is in flight
+                        // while chunk j is replayed
+                        const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + hn * 128);
+                        uint32_t ca[16], cb[16];
+                        if constexpr (MODE == CE_SUPPLIED_TILES) {
+                            ce_load_supplied(P.tiles_in, tile_id, row, hn * 128, ca);
+                        } else {
+                            tmem_ld16(trow, ca);
+                            ce_wait_ld(ca);
+                        }
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float msf = __uint_as_float(ms[i]);
-                            uint32_t acc_i = 0;
-#pragma unroll
-                            for (int half = 0; half < 2; ++half) {
-                                // 16 count columns (weight row 4 hn + i, slots 16 half ..) per pass
-                                const int col0 = (4 * hn + i) * 32 + half * 16;
-                                uint32_t c[16];
-                                if constexpr (MODE == CE_SUPPLIED_TILES) {
-                                    const int4* src =
-                                        reinterpret_cast<const int4*>(P.tiles_in + (tile_id * 128 + row) * 256 + col0);
-#pragma unroll
-                                    for (int v = 0; v < 4; ++v) {
-                                        const int4 x = src[v];
-                                        c[4 * v] = (uint32_t)x.x; c[4 * v + 1] = (uint32_t)x.y;
-                                        c[4 * v + 2] = (uint32_t)x.z; c[4 * v + 3] = (uint32_t)x.w;
-                                    }
-                                } else {
-                                    tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + col0), c);
-                                    tmem_wait_ld();
-                                }
-                                if constexpr (MODE == CE_DUMP_TILES) {
-                                    int4* dst = reinterpret_cast<int4*>(P.tiles_out + (tile_id * 128 + row) * 256 + col0);
-#pragma unroll
-                                    for (int v = 0; v < 4; ++v)
-                                        dst[v] = make_int4((int)c[4 * v], (int)c[4 * v + 1], (int)c[4 * v + 2],
-                                                           (int)c[4 * v + 3]);
-                                }
-                                const float4* fb4 = reinterpret_cast<const float4*>(FB + tb * 256 + col0);
-                                const uint4* rr4 = reinterpret_cast<const uint4*>(RR + tb * 256 + col0);
-#pragma unroll
-                                for (int v = 0; v < 4; ++v) {
-                                    const float4 fb = fb4[v];
-                                    const uint4 rr = rr4[v];
-                                    acc_i += c[4 * v] * __float_as_uint(__fmaf_rz(fa_abs, fb.x, msf));
-                                    acc_i += c[4 * v + 1] * __float_as_uint(__fmaf_rz(fa_abs, fb.y, msf));
-                                    acc_i += c[4 * v + 2] * __float_as_uint(__fmaf_rz(fa_abs, fb.z, msf));
-                                    acc_i += c[4 * v + 3] * __float_as_uint(__fmaf_rz(fa_abs, fb.w, msf));
-                                    fp += c[4 * v] * rr.x + c[4 * v + 1] * rr.y + c[4 * v + 2] * rr.z + c[4 * v + 3] * rr.w;
-                                }
+                        for (int chunk = 0; chunk < 8; ++chunk) {
+                            uint32_t (&cur)[16] = (chunk & 1) ? cb : ca;
+                            uint32_t (&nxt)[16] = (chunk & 1) ? ca : cb;
+                            if (chunk < 7) {
+                                if constexpr (MODE == CE_SUPPLIED_TILES)
+                                    ce_load_supplied(P.tiles_in, tile_id, row, hn * 128 + (chunk + 1) * 16, nxt);
+                                else
+                                    tmem_ld16(trow + (uint32_t)((chunk + 1) * 16), nxt);
                             }
-                            part[i] = acc_i;
+                            const int col0 = hn * 128 + chunk * 16;
+                            if constexpr (MODE == CE_DUMP_TILES) {
+                                int4* dst = reinterpret_cast<int4*>(P.tiles_out + (tile_id * 128 + row) * 256 + col0);
+#pragma unroll
+                                for (int v = 0; v < 4; ++v)
+                                    dst[v] = make_int4((int)cur[4 * v], (int)cur[4 * v + 1], (int)cur[4 * v + 2],
+                                                       (int)cur[4 * v + 3]);
+                            }
+                            const float msf = __uint_as_float(ms[chunk >> 1]);
+                            const float4* fb4 = reinterpret_cast<const float4*>(FB + col0);
+                            const uint4* rr4 = reinterpret_cast<const uint4*>(RR + col0);
+                            uint32_t acc_c = 0;
+#pragma unroll
+                            for (int v = 0; v < 4; ++v) {
+                                const float4 fb = fb4[v];
+                                const uint4 rr = rr4[v];
+                                acc_c += cur[4 * v] * __float_as_uint(__fmaf_rz(fa_abs, fb.x, msf));
+                                acc_c += cur[4 * v + 1] * __float_as_uint(__fmaf_rz(fa_abs, fb.y, msf));
+                                acc_c += cur[4 * v + 2] * __float_as_uint(__fmaf_rz(fa_abs, fb.z, msf));
+                                acc_c += cur[4 * v + 3] * __float_as_uint(__fmaf_rz(fa_abs, fb.w, msf));
+                                fp += cur[4 * v] * rr.x + cur[4 * v + 1] * rr.y + cur[4 * v + 2] * rr.z +
+                                      cur[4 * v + 3] * rr.w;
+                            }
+                            part[chunk >> 1] += acc_c;
+                            if constexpr (MODE != CE_SUPPLIED_TILES) {
+                                if (chunk < 7) ce_wait_ld(nxt);
+                            }
                         }
                         // the counts are in registers: hand the tensor-memory tile back
                         tc_fence_before();
@@ -645,8 +669,8 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                             const unsigned char* As = smem + CE_OFF_A + abuf * CE_A_BYTES;
                             const uint4 a0 = *reinterpret_cast<const uint4*>(As + ce_sw64((uint32_t)row, 2 * h));
                             const uint4 a1 = *reinterpret_cast<const uint4*>(As + ce_sw64((uint32_t)row, 2 * h + 1));
-                            const uint4* br1 = reinterpret_cast<const uint4*>(BR + ((tb * 2 + hn) * 2 + 0) * 32);
-                            const uint4* br2 = reinterpret_cast<const uint4*>(BR + ((tb * 2 + hn) * 2 + 1) * 32);
+                            const uint4* br1 = reinterpret_cast<const uint4*>(BR + (hn * 2 + 0) * 32);
+                            const uint4* br2 = reinterpret_cast<const uint4*>(BR + (hn * 2 + 1) * 32);
                             const uint4 x0 = br1[0], x1 = br1[1], y0 = br2[0], y1 = br2[1];
                             int e1 = 0, e2 = 0;
                             e1 = __dp4a((int)a0.x, (int)x0.x, e1); e1 = __dp4a((int)a0.y, (int)x0.y, e1);
@@ -668,7 +692,7 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                         if ((lane >> 2) == t) {
                             const uint32_t m = ms_own;
                             const uint32_t total = own_i == 0 ? tot[0] : own_i == 1 ? tot[1] : own_i == 2 ? tot[2] : tot[3];
-                            const int pn = PN[tb * 32 + own_o];
+                            const int pn = PN[own_o];
                             const uint32_t amask = (uint32_t)((int32_t)__float_as_uint(acc) >> 31);
                             const uint32_t av = __float_as_uint(__fmaf_rz(fabsf(acc), 1.0f, __uint_as_float(m))) - m;
                             const uint32_t T = ((av ^ amask) - amask) + total - m * (uint32_t)pn;
@@ -680,7 +704,7 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                     }
                     if (!ok) break;
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&b_empty[ubuf]);
+                    if (lane == 0) mbar_arrive(&b_empty[slot]);
                 }
                 if (!ok) break;
                 __syncwarp();
@@ -728,6 +752,24 @@ int ima_class_count_prepare(const uint8_t* fp8, int64_t rows, int64_t K, int64_t
     return IMA_LAUNCH_STATUS();
 }
 
+int64_t ima_class_count_weight_tiles_bytes(int64_t N, int64_t K) {
+    if (N <= 0 || K <= 0) return 0;
+    return ((N + CE_TN - 1) / CE_TN) * ((ce_groups(K) + 1) / 2) * (int64_t)CE_RECORD;
+}
+
+int ima_class_count_weight_tiles(const void* w_operand, int64_t N, int64_t K, uint64_t seed, void* tiles,
+                                 void* stream) {
+    if (!w_operand || !tiles || N < 0 || K < 0) return IMA_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(w_operand) & 15) || (reinterpret_cast<uintptr_t>(tiles) & 15))
+        return IMA_ERR_INVALID_ARGUMENT;
+    if (N == 0 || K == 0) return IMA_OK;
+    const int64_t ntiles = (N + CE_TN - 1) / CE_TN, gp = (ce_groups(K) + 1) / 2;
+    if (gp > 65535) return IMA_ERR_UNSUPPORTED;
+    ce_weight_tiles_kernel<<<dim3((unsigned)ntiles, (unsigned)gp), 256, 0, (cudaStream_t)stream>>>(
+        ce_operand(w_operand, N, K), gp, seed, reinterpret_cast<unsigned char*>(tiles));
+    return IMA_LAUNCH_STATUS();
+}
+
 int64_t ima_class_count_tile_entries(int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     const int64_t strips = ((M + CE_TM - 1) / CE_TM) * ((N + CE_STRIP_N - 1) / CE_STRIP_N);
@@ -735,21 +777,24 @@ int64_t ima_class_count_tile_entries(int64_t M, int64_t N, int64_t K) {
     return strips * gp * CE_MAX_TILES * 2 * 128 * 256;
 }
 
-int ima_class_count_replay(const void* x_operand, const void* w_operand, const float* x_scale, const float* w_scale,
-                           int64_t M, int64_t N, int64_t K, uint64_t seed, uint16_t* out_bf16, int64_t ld_bf16,
+int ima_class_count_replay(const void* x_operand, const void* w_operand, const void* w_tiles, const float* x_scale,
+                           const float* w_scale, int64_t M, int64_t N, int64_t K, uint16_t* out_bf16, int64_t ld_bf16,
                            float* out_f32, int64_t ld_f32, int32_t* mismatch_rows, int32_t* tiles_out,
                            const int32_t* tiles_in, void* stream) {
-    if (!x_operand || !w_operand || !x_scale || !w_scale || !mismatch_rows || M < 0 || N < 0 || K < 0)
+    if (!x_operand || !w_operand || !w_tiles || !x_scale || !w_scale || !mismatch_rows || M < 0 || N < 0 || K < 0)
         return IMA_ERR_INVALID_ARGUMENT;
     if (!out_bf16 && !out_f32) return IMA_ERR_INVALID_ARGUMENT;
     if ((out_bf16 && ld_bf16 < N) || (out_f32 && ld_f32 < N)) return IMA_ERR_INVALID_ARGUMENT;
     if ((reinterpret_cast<uintptr_t>(x_operand) & 15) || (reinterpret_cast<uintptr_t>(w_operand) & 15) ||
-        (reinterpret_cast<uintptr_t>(tiles_out) & 15) || (reinterpret_cast<uintptr_t>(tiles_in) & 15))
+        (reinterpret_cast<uintptr_t>(w_tiles) & 15) || (reinterpret_cast<uintptr_t>(tiles_out) & 15) ||
+        (reinterpret_cast<uintptr_t>(tiles_in) & 15))
         return IMA_ERR_INVALID_ARGUMENT;
+    if (tiles_out && tiles_in) return IMA_ERR_INVALID_ARGUMENT;
     if (M == 0 || N == 0) return IMA_OK;
     CeParams p;
     p.a = ce_operand(x_operand, M, K);
     p.b = ce_operand(w_operand, N, K);
+    p.w_tiles = reinterpret_cast<const unsigned char*>(w_tiles);
     p.xs = x_scale;
     p.ws = w_scale;
     p.M = M;
@@ -764,9 +809,6 @@ int ima_class_count_replay(const void* x_operand, const void* w_operand, const f
     p.mismatch = mismatch_rows;
     p.tiles_out = tiles_out;
     p.tiles_in = tiles_in;
-    p.seed = seed;
-    const int64_t strips = p.strips_m * p.strips_n;
-    if (tiles_out && tiles_in) return IMA_ERR_INVALID_ARGUMENT;
     auto kern = tiles_in ? class_count_replay_kernel<CE_SUPPLIED_TILES>
                          : tiles_out ? class_count_replay_kernel<CE_DUMP_TILES> : class_count_replay_kernel<CE_TENSOR_COUNTS>;
     int rc = ima_note_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CE_ALLOC));
@@ -778,6 +820,7 @@ int ima_class_count_replay(const void* x_operand, const void* w_operand, const f
             rc = ima_note_cuda(cudaMemset2DAsync(out_f32, ld_f32 * 4, 0, N * 4, M, (cudaStream_t)stream));
         return rc;
     }
+    const int64_t strips = p.strips_m * p.strips_n;
     const int grid = (int)(strips < num_sms() ? strips : num_sms());
     kern<<<grid, CE_THREADS, CE_ALLOC, (cudaStream_t)stream>>>(p);
     return IMA_LAUNCH_STATUS();

@@ -290,12 +290,18 @@ def class_count_stats(
     )
 
 
+_SEED_COUNTER = [0x5EED]
+
+
 class ClassCountOperand:
     """An e4m3 matrix [rows, K] staged for the class-count engine: per row and group of 32 k,
     the slot of each element's class among the row's classes in the group, the classes'
-    codes, exponent pairs and present/sign masks (ima_class_count_prepare)."""
+    codes, exponent pairs and present/sign masks (ima_class_count_prepare).  A weight
+    (weight=True) is also expanded into its tile records (ima_class_count_weight_tiles): the
+    one-hot weight slot rows, class magnitudes and the fingerprint weights, drawn from `seed`
+    (a fresh one per staging when None)."""
 
-    def __init__(self, fp8: torch.Tensor):
+    def __init__(self, fp8: torch.Tensor, *, weight: bool = False, seed: int | None = None):
         if fp8.device.type != "cuda":
             raise RuntimeError("Hawkeye class-count replay is CUDA-only")
         raw = fp8.contiguous().view(torch.uint8)
@@ -306,6 +312,16 @@ class ClassCountOperand:
         with torch.cuda.device(raw.device):
             nat.call("ima_class_count_prepare", raw.data_ptr(), self.rows, self.k, self.k, self.buffer.data_ptr(),
                      nat.stream_of(raw.device))
+        self.tiles = None
+        if weight:
+            if seed is None:
+                _SEED_COUNTER[0] += 1
+                seed = _SEED_COUNTER[0] * 0x9E3779B97F4A7C15 % (1 << 64)
+            tbytes = int(nat.lib().ima_class_count_weight_tiles_bytes(self.rows, self.k))
+            self.tiles = torch.empty((max(tbytes, 16),), dtype=torch.uint8, device=raw.device)
+            with torch.cuda.device(raw.device):
+                nat.call("ima_class_count_weight_tiles", self.buffer.data_ptr(), self.rows, self.k,
+                         int(seed) % (1 << 64), self.tiles.data_ptr(), nat.stream_of(raw.device))
         self._source = fp8
         self._version = nat.tensor_version(fp8)
         self._data_ptr = fp8.data_ptr()
@@ -331,15 +347,12 @@ def stage_class_count_weight(w_fp8: torch.Tensor) -> ClassCountOperand:
     cached = getattr(w_fp8, "_ima_class_count_operand", None)
     if cached is not None and cached.matches(w_fp8):
         return cached
-    op = ClassCountOperand(w_fp8)
+    op = ClassCountOperand(w_fp8, weight=True)
     try:
         w_fp8._ima_class_count_operand = op
     except (AttributeError, RuntimeError):
         pass
     return op
-
-
-_SEED_COUNTER = [0x5EED]
 
 
 def class_count_replay(
@@ -348,7 +361,6 @@ def class_count_replay(
     x_scale: torch.Tensor,
     w_scale: torch.Tensor,
     *,
-    seed: int | None = None,
     out: torch.Tensor | None = None,
     out_f32: torch.Tensor | None = None,
     mismatch: torch.Tensor | None = None,
@@ -362,6 +374,8 @@ def class_count_replay(
     m, n, k = x_op.rows, w_op.rows, x_op.k
     if w_op.k != k:
         raise RuntimeError(f"Hawkeye shape mismatch: K={k} vs K={w_op.k}")
+    if w_op.tiles is None:
+        raise RuntimeError("the weight operand was staged without its tile records (ClassCountOperand(w, weight=True))")
     dev = x_op.device
     xs = x_scale.reshape(-1).to(torch.float32).contiguous()
     ws = w_scale.reshape(-1).to(torch.float32).contiguous()
@@ -375,16 +389,15 @@ def class_count_replay(
     for label, t in (("tiles_out", tiles_out), ("tiles_in", tiles_in)):
         if t is not None and (t.dtype != torch.int32 or t.numel() < entries or not t.is_contiguous()):
             raise RuntimeError(f"{label} must be a contiguous int32 tensor of at least {entries} entries")
-    nat.require_device(dev, ("weight operand", w_op.buffer), ("x_scale", xs), ("w_scale", ws), ("output", out),
+    nat.require_device(dev, ("weight operand", w_op.buffer), ("weight tiles", w_op.tiles), ("x_scale", xs),
+                       ("w_scale", ws), ("output", out),
                        ("fp32 output", out_f32), ("mismatch counter", mismatch), ("tiles_out", tiles_out),
                        ("tiles_in", tiles_in))
-    if seed is None:
-        _SEED_COUNTER[0] += 1
-        seed = _SEED_COUNTER[0] * 0x9E3779B97F4A7C15 % (1 << 64)
     with torch.cuda.device(dev):
         nat.call(
-            "ima_class_count_replay", x_op.buffer.data_ptr(), w_op.buffer.data_ptr(), xs.data_ptr(), ws.data_ptr(),
-            m, n, k, int(seed) % (1 << 64), nat.ptr(out), out.stride(0) if out is not None else n, nat.ptr(out_f32),
+            "ima_class_count_replay", x_op.buffer.data_ptr(), w_op.buffer.data_ptr(), w_op.tiles.data_ptr(),
+            xs.data_ptr(), ws.data_ptr(), m, n, k, nat.ptr(out), out.stride(0) if out is not None else n,
+            nat.ptr(out_f32),
             out_f32.stride(0) if out_f32 is not None else n, mismatch.data_ptr(), nat.ptr(tiles_out),
             nat.ptr(tiles_in), nat.stream_of(dev),
         )

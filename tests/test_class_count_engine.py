@@ -33,7 +33,7 @@ def _case(m, k, n, seed, outliers=0.01):
 
 def _engine(xq, xs, w, ws, device, **kw):
     x_op = hawkeye_freivalds.ClassCountOperand(xq.to(device))
-    w_op = hawkeye_freivalds.ClassCountOperand(w.to(device))
+    w_op = hawkeye_freivalds.ClassCountOperand(w.to(device), weight=True)
     out, bad = hawkeye_freivalds.class_count_replay(x_op, w_op, xs.to(device), ws.to(device), **kw)
     torch.cuda.synchronize()
     return out, int(bad.item()), x_op, w_op
