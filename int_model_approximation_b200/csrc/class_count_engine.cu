@@ -45,12 +45,15 @@
 //
 // CTA (one per SM, persistent over "strips" of 4 tokens x 64 weight rows, all groups):
 //   warp 0     TMEM allocation (512 columns: two 256-column count tiles) and MMA issue
-//   warps 1-3  operand builders: one-hot A (per group pair) and B (per tile) in shared memory
-//              with the 64-byte swizzle, the class tables, the fingerprint vectors and each
-//              output's present-exponent maximum and signed present count
-//   warps 4-11 epilogue: warp (q = warp % 4, half) reads TMEM lanes 32q.. (token q of the
-//              strip) and half of the 8 weight rows of a tile; lane j keeps the accumulator of
-//              one output per tile
+//   warp 1     loader: bulk copies of each unit's operands (the weight tile record of
+//              ima_class_count_weight_tiles -- one-hot weight slot rows in the 64-byte swizzle,
+//              class magnitudes, fingerprint weights -- and the tokens' and weight rows' staged
+//              records) into one of four unit buffers, up to four units ahead
+//   warps 2-3  builders: the one-hot token slot rows per group pair, and each output's
+//              present-exponent maximum and signed present count per unit
+//   warps 4-19 epilogue: warp (q = warp % 4, part) reads TMEM lanes 32q.. (token q of the
+//              strip) and the count columns of 2 of the 8 weight rows of a tile; lane j < 16
+//              keeps the accumulator of one output (tile j / 2)
 // Every mbarrier wait is bounded and abort-aware; the MMA thread drains its work before the
 // CTA frees tensor memory.
 #include "sm100_primitives.cuh"
@@ -60,11 +63,14 @@ namespace {
 constexpr int CE_GROUP = 32;
 constexpr int CE_TM = 4;                       // token rows per MMA tile: 4 x 32 slot rows = M 128
 constexpr int CE_TN = 8;                       // weight rows per MMA tile: 8 x 32 slot rows = N 256
+constexpr int CE_TN_CONST = CE_TN;
 constexpr int CE_MAX_TILES = 8;                // MMA tiles per strip
 constexpr int CE_STRIP_N = CE_TN * CE_MAX_TILES;
 constexpr int CE_PITCH = 64;                   // staged rows are padded to a multiple of this
 constexpr int CE_BUILD_WARPS = 2;
-constexpr int CE_EPI_WARPS = 8;
+constexpr int CE_EPI_WARPS = 16;                // four per TMEM lane quadrant
+constexpr int CE_PARTS = CE_EPI_WARPS / 4;      // column parts of a tile, one per warp of a quadrant
+constexpr int CE_NLW = CE_TN_CONST / CE_PARTS;  // weight rows per epilogue warp and tile
 constexpr int CE_BUILDERS = 32 * CE_BUILD_WARPS;
 constexpr int CE_FIRST_EPI_WARP = 2 + CE_BUILD_WARPS;   // warp 0 MMA, warp 1 loader, then builders
 constexpr int CE_THREADS = 32 * (CE_FIRST_EPI_WARP + CE_EPI_WARPS);
@@ -79,8 +85,8 @@ constexpr int CE_UNITS = 4;                    // unit buffers in shared memory 
 constexpr int CE_R_B = 0;                      // one-hot weight slot rows [256][64 B], 64-byte swizzle
 constexpr int CE_R_FB = 256 * 64;              // f32 [2 h][256]: |s| 2^e of each slot column's class
 constexpr int CE_R_RR = CE_R_FB + 2 * 256 * 4; // u32 [2][256]: fingerprint weights r1 + 2^16 r2
-constexpr int CE_R_BR = CE_R_RR + 2 * 256 * 4; // s8 [2 h][2 half][2 vec][32 k]: B^T r per half tile
-constexpr int CE_RECORD = CE_R_BR + 2 * 2 * 2 * 32;   // 20736 bytes
+constexpr int CE_R_BR = CE_R_RR + 2 * 256 * 4; // s8 [2 h][CE_PARTS][2 vec][32 k]: B^T r per column part
+constexpr int CE_RECORD = CE_R_BR + 2 * CE_PARTS * 2 * 32;
 // unit buffer in shared memory: the weight record, then the per-unit staging and tables
 constexpr int CE_U_EXB = CE_RECORD;                    // u32 [2 h][8][16] exponent pairs of the 8 weight rows
 constexpr int CE_U_PSB = CE_U_EXB + 2 * CE_TN * 64;    // uint4 [2][8] masks
@@ -230,12 +236,12 @@ __global__ void __launch_bounds__(256) ce_weight_tiles_kernel(CeOperand B, int64
         RR[i] = ce_fingerprint_weight(seed, tile * 2 + h, (uint32_t)col);
     }
     int8_t* BR = reinterpret_cast<int8_t*>(rec + CE_R_BR);
-    for (int i = threadIdx.x; i < 2 * 2 * 32; i += blockDim.x) {
-        const int h = i >> 6, half = (i >> 5) & 1, k = i & 31;
+    for (int i = threadIdx.x; i < 2 * CE_PARTS * 32; i += blockDim.x) {
+        const int h = i / (CE_PARTS * 32), part = (i >> 5) % CE_PARTS, k = i & 31;
         const int64_t g = 2 * gp + h;
         int s1 = 0, s2 = 0;
         if (g < G) {
-            for (int nl = half * 4; nl < half * 4 + 4; ++nl) {
+            for (int nl = part * CE_NLW; nl < part * CE_NLW + CE_NLW; ++nl) {
                 const int64_t r = g * B.pitch + n0 + nl;
                 const uint32_t slot = B.sl[r * 32 + k];
                 if (slot == CE_NO_SLOT) continue;
@@ -245,8 +251,8 @@ __global__ void __launch_bounds__(256) ce_weight_tiles_kernel(CeOperand B, int64
                 s2 += neg ? -(int)(rr >> 16) : (int)(rr >> 16);
             }
         }
-        BR[((h * 2 + half) * 2 + 0) * 32 + k] = (int8_t)s1;
-        BR[((h * 2 + half) * 2 + 1) * 32 + k] = (int8_t)s2;
+        BR[((h * CE_PARTS + part) * 2 + 0) * 32 + k] = (int8_t)s1;
+        BR[((h * CE_PARTS + part) * 2 + 1) * 32 + k] = (int8_t)s2;
     }
 }
 
@@ -562,7 +568,7 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
     } else {
         // ---------------- epilogue: replay from the counts ----------------
         const int q = warp & 3;                      // token of the strip = TMEM lane quadrant
-        const int hn = (warp - CE_FIRST_EPI_WARP) >> 2;   // which 4 of a tile's 8 weight rows
+        const int part = (warp - CE_FIRST_EPI_WARP) >> 2;   // weight rows part*NLW .. of each tile
         const unsigned FULL = 0xFFFFFFFFu;
         const float* FA = reinterpret_cast<const float*>(smem + CE_OFF_FA);
         const int row = q * 32 + lane;               // this thread's slot row of the MMA tile
@@ -572,7 +578,7 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
             const int64_t m0 = (sid % P.strips_m) * CE_TM;
             const int64_t n0 = (sid / P.strips_m) * CE_STRIP_N;
             const int tiles = (int)min((int64_t)CE_MAX_TILES, (P.N - n0 + CE_TN - 1) / CE_TN);
-            float acc = 0.0f;                        // lane j: output (m0 + q, n0 + 8 (j >> 2) + 4 hn + (j & 3))
+            float acc = 0.0f;   // lane j < 8 NLW: output (m0 + q, n0 + 8 (j / NLW) + NLW part + j % NLW)
             for (int64_t gp = 0; gp < GP && ok; ++gp) {
                 const uint32_t abuf = a_cnt & 1u, aph = (a_cnt >> 1) & 1u;
                 ++a_cnt;
@@ -592,46 +598,49 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                         __syncwarp();
                         if (!__all_sync(FULL, ok)) { ok = false; break; }
                         tc_fence_after();
-                        // M_S of this warp's four outputs of the tile (owner lanes 4t .. 4t + 3)
-                        const int own_i = lane & 3;
-                        const int own_o = q * 8 + 4 * hn + own_i;
+                        // M_S of this warp's NLW outputs of the tile (owner lanes NLW t ..)
+                        const int own_i = lane % CE_NLW;
+                        const int own_o = q * 8 + CE_NLW * part + own_i;
                         const float* FB = reinterpret_cast<const float*>(U + CE_R_FB) + h * 256;
                         const uint32_t* RR = reinterpret_cast<const uint32_t*>(U + CE_R_RR) + h * 256;
-                        const int8_t* BR = reinterpret_cast<const int8_t*>(U + CE_R_BR) + h * 128;
+                        const int8_t* BR = reinterpret_cast<const int8_t*>(U + CE_R_BR) + h * CE_PARTS * 64;
                         const int32_t* PE = reinterpret_cast<const int32_t*>(U + CE_U_PE) + h * 32;
                         const int32_t* PN = reinterpret_cast<const int32_t*>(U + CE_U_PN) + h * 32;
                         const int pe = PE[own_o];
                         const int acc_e14 = (int)((__float_as_uint(acc) << 1) >> 24) - 133;
                         const uint32_t ms_own = (uint32_t)max(pe, acc_e14) * (1u << 23) + ((143u << 23) | 0x400000u);
-                        uint32_t ms[4];
+                        uint32_t ms[CE_NLW];
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) ms[i] = __shfl_sync(FULL, ms_own, t * 4 + i);
+                        for (int i = 0; i < CE_NLW; ++i) ms[i] = __shfl_sync(FULL, ms_own, t * CE_NLW + i);
                         const float fa = FA[(abuf * 2 + h) * 128 + row];
                         const float fa_abs = fabsf(fa);
-                        uint32_t part[4] = {0u, 0u, 0u, 0u}, fp = 0;
+                        uint32_t psum[CE_NLW], fp = 0;
+#pragma unroll
+                        for (int i = 0; i < CE_NLW; ++i) psum[i] = 0u;
                         const int64_t tile_id = (((sid * GP + gp) * CE_MAX_TILES + t) * 2 + h);
-                        // 8 chunks of 16 count columns (weight row 4 hn + (chunk >> 1), slots
+                        // 2 NLW chunks of 16 count columns (weight row NLW part + (chunk >> 1), slots
                         // 16 (chunk & 1) ..): the tensor-memory load of chunk j + 1 is in flight
                         // while chunk j is replayed
-                        const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + hn * 128);
+                        constexpr int CHUNKS = 2 * CE_NLW, PCOLS = 256 / CE_PARTS;
+                        const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + part * PCOLS);
                         uint32_t ca[16], cb[16];
                         if constexpr (MODE == CE_SUPPLIED_TILES) {
-                            ce_load_supplied(P.tiles_in, tile_id, row, hn * 128, ca);
+                            ce_load_supplied(P.tiles_in, tile_id, row, part * PCOLS, ca);
                         } else {
                             tmem_ld16(trow, ca);
                             ce_wait_ld(ca);
                         }
 #pragma unroll
-                        for (int chunk = 0; chunk < 8; ++chunk) {
+                        for (int chunk = 0; chunk < CHUNKS; ++chunk) {
                             uint32_t (&cur)[16] = (chunk & 1) ? cb : ca;
                             uint32_t (&nxt)[16] = (chunk & 1) ? ca : cb;
-                            if (chunk < 7) {
+                            if (chunk < CHUNKS - 1) {
                                 if constexpr (MODE == CE_SUPPLIED_TILES)
-                                    ce_load_supplied(P.tiles_in, tile_id, row, hn * 128 + (chunk + 1) * 16, nxt);
+                                    ce_load_supplied(P.tiles_in, tile_id, row, part * PCOLS + (chunk + 1) * 16, nxt);
                                 else
                                     tmem_ld16(trow + (uint32_t)((chunk + 1) * 16), nxt);
                             }
-                            const int col0 = hn * 128 + chunk * 16;
+                            const int col0 = part * PCOLS + chunk * 16;
                             if constexpr (MODE == CE_DUMP_TILES) {
                                 int4* dst = reinterpret_cast<int4*>(P.tiles_out + (tile_id * 128 + row) * 256 + col0);
 #pragma unroll
@@ -654,9 +663,9 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                                 fp += cur[4 * v] * rr.x + cur[4 * v + 1] * rr.y + cur[4 * v + 2] * rr.z +
                                       cur[4 * v + 3] * rr.w;
                             }
-                            part[chunk >> 1] += acc_c;
+                            psum[chunk >> 1] += acc_c;
                             if constexpr (MODE != CE_SUPPLIED_TILES) {
-                                if (chunk < 7) ce_wait_ld(nxt);
+                                if (chunk < CHUNKS - 1) ce_wait_ld(nxt);
                             }
                         }
                         // the counts are in registers: hand the tensor-memory tile back
@@ -669,8 +678,8 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                             const unsigned char* As = smem + CE_OFF_A + abuf * CE_A_BYTES;
                             const uint4 a0 = *reinterpret_cast<const uint4*>(As + ce_sw64((uint32_t)row, 2 * h));
                             const uint4 a1 = *reinterpret_cast<const uint4*>(As + ce_sw64((uint32_t)row, 2 * h + 1));
-                            const uint4* br1 = reinterpret_cast<const uint4*>(BR + (hn * 2 + 0) * 32);
-                            const uint4* br2 = reinterpret_cast<const uint4*>(BR + (hn * 2 + 1) * 32);
+                            const uint4* br1 = reinterpret_cast<const uint4*>(BR + (part * 2 + 0) * 32);
+                            const uint4* br2 = reinterpret_cast<const uint4*>(BR + (part * 2 + 1) * 32);
                             const uint4 x0 = br1[0], x1 = br1[1], y0 = br2[0], y1 = br2[1];
                             int e1 = 0, e2 = 0;
                             e1 = __dp4a((int)a0.x, (int)x0.x, e1); e1 = __dp4a((int)a0.y, (int)x0.y, e1);
@@ -684,14 +693,16 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
                             const uint32_t expect = (uint32_t)e1 + ((uint32_t)e2 << 16);
                             if (fp != expect) atomicAdd(P.mismatch, 1);
                         }
-                        // sum sgn_a * part over the 32 slot rows of the token: one REDUX per weight row
+                        // sum sgn_a * psum over the 32 slot rows of the token: one REDUX per weight row
                         const uint32_t neg = fa < 0.0f ? 0xFFFFFFFFu : 0u;
-                        uint32_t tot[4];
+                        uint32_t total = 0;
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) tot[i] = __reduce_add_sync(FULL, (part[i] ^ neg) - neg);
-                        if ((lane >> 2) == t) {
+                        for (int i = 0; i < CE_NLW; ++i) {
+                            const uint32_t tot = __reduce_add_sync(FULL, (psum[i] ^ neg) - neg);
+                            if (own_i == i) total = tot;
+                        }
+                        if (lane / CE_NLW == t) {
                             const uint32_t m = ms_own;
-                            const uint32_t total = own_i == 0 ? tot[0] : own_i == 1 ? tot[1] : own_i == 2 ? tot[2] : tot[3];
                             const int pn = PN[own_o];
                             const uint32_t amask = (uint32_t)((int32_t)__float_as_uint(acc) >> 31);
                             const uint32_t av = __float_as_uint(__fmaf_rz(fabsf(acc), 1.0f, __uint_as_float(m))) - m;
@@ -713,8 +724,8 @@ __global__ void __launch_bounds__(CE_THREADS, 1) class_count_replay_kernel(const
             if (!ok) break;
             // outputs of the strip: gfloat = acc * 2^-20, y = (gfloat * xs) * ws
             const int64_t m = m0 + q;
-            const int64_t n = n0 + 8 * (lane >> 2) + 4 * hn + (lane & 3);
-            if ((lane >> 2) < tiles && m < P.M && n < P.N) {
+            const int64_t n = n0 + 8 * (lane / CE_NLW) + CE_NLW * part + (lane % CE_NLW);
+            if (lane / CE_NLW < tiles && m < P.M && n < P.N) {
                 const float gf = __fmul_rn(acc, 9.5367431640625e-07f);
                 const float y = __fmul_rn(__fmul_rn(gf, P.xs[m]), P.ws[n]);
                 if (P.out_bf16) P.out_bf16[m * P.ld_bf16 + n] = __float2bfloat16_rn(y);
