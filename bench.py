@@ -1357,7 +1357,7 @@ def c4_cpu_baseline(specs, stacks, xs, sets, layers: int, budget_s: float) -> di
 
 def c4_hawkeye_phase(args, specs, xs, world: int, rank: int, device) -> dict:
     """Config 4 through the direct Hawkeye replay: per layer, quantise and stage the seven
-    activations, replay the seven linears (round-robin on four side streams), gather the bf16
+    activations (one fused launch each), replay the seven linears (round-robin on four side streams), gather the bf16
     outputs (NCCL all-gather per linear at N > 1).  Timed on the device, max over ranks."""
     from int_model_approximation_b200 import _native as nat
     from int_model_approximation_b200 import synthetic
@@ -1395,10 +1395,9 @@ def c4_hawkeye_phase(args, specs, xs, world: int, rank: int, device) -> dict:
             sp_ = cs.cuda_stream
             for p, sp in enumerate(specs):
                 rows, k = sp["rows"], sp["k"]
-                nat.check("q", lib.ima_quantize_per_token(xs[p].data_ptr(), nat.IMA_DTYPE_BF16, rows, k, k,
-                                                          q[p].data_ptr(), k, scale[p].data_ptr(), None, k, None,
-                                                          None, 16, sp_))
-                nat.check("p", lib.ima_hawkeye_prepare(q[p].data_ptr(), rows, k, k, xop[p].data_ptr(), sp_))
+                nat.check("qp", lib.ima_hawkeye_quantize_prepare(xs[p].data_ptr(), nat.IMA_DTYPE_BF16, rows, k, k,
+                                                                 scale[p].data_ptr(), q[p].data_ptr(), k,
+                                                                 xop[p].data_ptr(), sp_))
             for st in side:
                 st.wait_stream(cs)
             for p, sp in enumerate(specs):

@@ -201,6 +201,15 @@ int ima_hawkeye_replay(const void* x_operand, const void* w_operand, const float
                        int64_t M, int64_t N, int64_t K, int products_per_group, int internal_width,
                        int zero_exponent, uint16_t* out_bf16, int64_t ld_bf16, float* out_f32, int64_t ld_f32,
                        void* stream);
+/* Activation side of one Hawkeye linear in one launch: per-token quantisation
+ * (ref: __main__.py:148-154 _fp8_per_token, the same bits as ima_quantize_per_token)
+ * fused with the staging of ima_hawkeye_prepare (ref: hawkeye.py:222-275 reads the
+ * quantised rows).  x [M, K] (row stride ldx elements, x_dtype IMA_DTYPE_*) ->
+ * scale[M] (fp32), the staged operand (ima_hawkeye_operand_bytes(M, K) bytes,
+ * identical to ima_hawkeye_prepare of the codes) and, when q_fp8 is not NULL, the
+ * e4m3 codes [M, K] (row stride ldq). */
+int ima_hawkeye_quantize_prepare(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, float* scale,
+                                 uint8_t* q_fp8, int64_t ldq, void* operand, void* stream);
 
 /* ---- A6: Freivalds check A (B r) == (A B) r, wrapping int64 ------------------
  * ref: tests/test_real_integer_gemms.py:67-93 (_exact_matvec /

@@ -115,6 +115,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ima_hawkeye_operand_pitch": (_I64, [_I64]),
     "ima_hawkeye_operand_bytes": (_I64, [_I64, _I64]),
     "ima_hawkeye_prepare": (_I32, [_VP, _I64, _I64, _I64, _VP, _VP]),
+    "ima_hawkeye_quantize_prepare": (_I32, [_VP, _I32, _I64, _I64, _I64, _VP, _VP, _I64, _VP, _VP]),
     "ima_hawkeye_replay": (
         _I32,
         [_VP, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _I32, _I32, _VP, _I64, _VP, _I64, _VP],

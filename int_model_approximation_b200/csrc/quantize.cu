@@ -363,6 +363,137 @@ __global__ void __launch_bounds__(256, 3) quantize_rows_kernel(const __grid_cons
     }
 }
 
+// Per-token quantisation fused with the Hawkeye operand staging (ima_hawkeye_quantize_prepare):
+// the row scale and the e4m3 codes exactly as quantize_rows_kernel computes them (the same
+// amax, scale, division and cast functions), written straight into the [k][row] records the
+// replay reads (hawkeye.cu's staged layout: per k the record {|s| 2^e as fp32 bits, sign mask},
+// per pair of k the int16 exponent pair, per group the sign word), and optionally the codes.
+// A block covers 32 rows.  Phase 1: 8 warps x 4 rows, the NaN-propagating amax and the scale.
+// Phase 2: thread (row = lane, warp) takes groups warp, warp + 8, ...: 32 elements -> 32 codes
+// -> records; for each k the block's 32 rows form one contiguous 256-byte store.
+constexpr int HQ_GROUP = 32;
+constexpr int HQ_ABSENT_EXP = -8192;
+
+__global__ void __launch_bounds__(256) hawkeye_quant_stage_kernel(const void* __restrict__ x, int dtype, int64_t M,
+                                                                  int64_t K, int64_t ldx, float* __restrict__ scale,
+                                                                  uint8_t* __restrict__ q, int64_t ldq, int64_t pitch,
+                                                                  int64_t groups, uint2* __restrict__ rec,
+                                                                  uint32_t* __restrict__ ex, uint32_t* __restrict__ sg) {
+    __shared__ float s_s[32], s_y[32];
+    __shared__ int s_mode[32];   // 1: fast path (finite scale, half input); 2: IEEE, finite scale; 0: IEEE, NaN/inf
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r0 = (int64_t)blockIdx.x * 32;
+    const bool half = dtype != IMA_DTYPE_F32, bf16 = dtype == IMA_DTYPE_BF16;
+    const int esz = half ? 2 : 4;
+    // ---- phase 1: row scales ----
+    for (int i = 0; i < 4; ++i) {
+        const int rl = warp * 4 + i;
+        const int64_t m = r0 + rl;
+        float amax = 0.0f;
+        int has_nan = 0;
+        if (m < M) {
+            const unsigned char* row = reinterpret_cast<const unsigned char*>(x) + m * ldx * esz;
+            const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+            if (half) {
+                uint32_t mx2 = 0;
+                const uint16_t* hrow = reinterpret_cast<const uint16_t*>(row);
+                for (int64_t k0 = (int64_t)lane * 8; k0 < K; k0 += 256) {
+                    const uint4 u = qz_load_half8(hrow, k0, K, vec);
+                    mx2 = qz_absmax2(mx2, u.x, bf16);
+                    mx2 = qz_absmax2(mx2, u.y, bf16);
+                    mx2 = qz_absmax2(mx2, u.z, bf16);
+                    mx2 = qz_absmax2(mx2, u.w, bf16);
+                }
+                const float a0 = qz_half_to_f32(mx2 & 0xFFFFu, bf16), a1 = qz_half_to_f32(mx2 >> 16, bf16);
+                has_nan = (a0 != a0) || (a1 != a1);
+                amax = fmaxf(a0, a1);
+            } else {
+                for (int64_t k0 = (int64_t)lane * 8; k0 < K; k0 += 256) {
+                    float v[8];
+                    load8(row, dtype, k0, K, vec, v);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float a = fabsf(v[j]);
+                        if (a != a) has_nan = 1;
+                        else amax = fmaxf(amax, a);
+                    }
+                }
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            has_nan |= __shfl_xor_sync(0xFFFFFFFFu, has_nan, o);
+        }
+        if (lane == 0) {
+            const float sc = qz_row_scale(has_nan ? __int_as_float(0x7FC00000) : amax);
+            const bool finite = fabsf(sc) <= 3.402823466e38f;
+            s_s[rl] = sc;
+            s_y[rl] = __frcp_rn(sc);
+            s_mode[rl] = (finite && half) ? 1 : (finite ? 2 : 0);
+            if (m < M) scale[m] = sc;
+        }
+    }
+    __syncthreads();
+    // ---- phase 2: codes and staged records ----
+    const int64_t m = r0 + lane;
+    const bool live = m < M;
+    const float sc = s_s[lane], y = s_y[lane];
+    const int mode = s_mode[lane];
+    const unsigned char* row = reinterpret_cast<const unsigned char*>(x) + (live ? m : 0) * ldx * esz;
+    const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+    for (int64_t g = warp; g < groups; g += 8) {
+        uint32_t codes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (live) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int64_t k0 = g * HQ_GROUP + c * 8;
+                if (k0 >= K) break;
+                float v[8];
+                uint2 qv;
+                if (mode == 1) {
+                    qz_unpack_half8(qz_load_half8(reinterpret_cast<const uint16_t*>(row), k0, K, vec), bf16, v);
+                    qv = qz_codes_fast(v, sc, y);   // columns beyond K load as +0: code 0
+                } else {
+                    load8(row, dtype, k0, K, vec, v);
+                    qv = qz_codes_ieee(v, sc, mode == 2, K - k0);
+                }
+                codes[2 * c] = qv.x;
+                codes[2 * c + 1] = qv.y;
+            }
+            if (q) {
+                uint8_t* qrow = q + m * ldq + g * HQ_GROUP;
+                const int64_t valid = K - g * HQ_GROUP;
+                if (valid >= HQ_GROUP && (reinterpret_cast<uintptr_t>(qrow) & 15) == 0) {
+                    reinterpret_cast<uint4*>(qrow)[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+                    reinterpret_cast<uint4*>(qrow)[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
+                } else {
+                    for (int j = 0; j < HQ_GROUP && j < valid; ++j) qrow[j] = (uint8_t)(codes[j >> 2] >> (8 * (j & 3)));
+                }
+            }
+        }
+        // the replay's operand records, element by element as ima_hawkeye_prepare writes them
+        uint32_t signs = 0, eprev = 0;
+#pragma unroll
+        for (int j = 0; j < HQ_GROUP; ++j) {
+            const int64_t k = g * HQ_GROUP + j;
+            const bool valid = live && k < K;
+            const uint32_t b = valid ? (codes[j >> 2] >> (8 * (j & 3))) & 0xFFu : 0u;
+            const uint32_t e_bits = (b >> 3) & 15u, mant = b & 7u;
+            const uint32_t sig = e_bits ? (mant | 8u) : mant;
+            const int e = e_bits ? (int)e_bits : 1;
+            const float mag = valid ? (float)sig * (float)(1u << e) : 0.0f;
+            const uint32_t mask = (valid && (b & 0x80u)) ? 0xFFFFFFFFu : 0u;
+            signs |= (mask & 1u) << j;
+            rec[(g * HQ_GROUP + j) * pitch + m] = make_uint2(__float_as_uint(mag), mask);
+            const int ev = (valid && sig != 0) ? e : HQ_ABSENT_EXP;
+            const uint32_t e16 = (uint32_t)ev & 0xFFFFu;
+            if (j & 1) ex[(g * (HQ_GROUP / 2) + (j >> 1)) * pitch + m] = eprev | (e16 << 16);
+            else eprev = e16;
+        }
+        sg[g * pitch + m] = signs;
+    }
+}
+
 // Self-test of the fast path (no reference counterpart; run by the GPU tests).
 //   kind 0: every fp32 value |f| < 464: hardware cvt vs ima_f32_to_e4m3
 //   kind 1 / 2: every positive finite bf16 (1) / fp16 (2) amax and every element x of
@@ -542,6 +673,22 @@ int ima_quantize_per_token(const void* x, int x_dtype, int64_t M, int64_t K, int
                            int8_t* planes, int64_t ldp, void* stream) {
     ima_quantize_problem q = {x, x_dtype, M, K, ldx, q_fp8, ldq, scale, codebook, ldc, code_scale, planes, ldp};
     return ima_quantize_grouped(&q, 1, stream);
+}
+
+int ima_hawkeye_quantize_prepare(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, float* scale,
+                                 uint8_t* q_fp8, int64_t ldq, void* operand, void* stream) {
+    if (!x || !scale || !operand || M < 0 || K < 0 || ldx < K) return IMA_ERR_INVALID_ARGUMENT;
+    if (x_dtype != IMA_DTYPE_F32 && x_dtype != IMA_DTYPE_BF16 && x_dtype != IMA_DTYPE_F16) return IMA_ERR_INVALID_ARGUMENT;
+    if (q_fp8 && ldq < K) return IMA_ERR_INVALID_ARGUMENT;
+    const int64_t pitch = ima_hawkeye_operand_pitch(M), groups = (K + HQ_GROUP - 1) / HQ_GROUP;
+    if (pitch == 0 || groups == 0) return IMA_OK;
+    if (pitch / 32 > INT32_MAX) return IMA_ERR_UNSUPPORTED;
+    uint2* rec = reinterpret_cast<uint2*>(operand);
+    uint32_t* ex = reinterpret_cast<uint32_t*>(rec + pitch * groups * HQ_GROUP);
+    uint32_t* sg = ex + pitch * groups * (HQ_GROUP / 2);
+    hawkeye_quant_stage_kernel<<<(unsigned)(pitch / 32), 256, 0, (cudaStream_t)stream>>>(
+        x, x_dtype, M, K, ldx, scale, q_fp8, ldq, pitch, groups, rec, ex, sg);
+    return IMA_LAUNCH_STATUS();
 }
 
 int ima_codebook_from_fp8(const uint8_t* src, int64_t rows, int64_t K, int64_t ld, int32_t* dst, int64_t ldd,

@@ -62,6 +62,38 @@ class HawkeyeOperand:
                 and fp8.data_ptr() == self._data_ptr)
 
 
+def quantize_and_stage(x: torch.Tensor, *, codes: bool = False):
+    """Per-token e4m3 quantisation of x [..., K] and its Hawkeye staging in one launch
+    (ima_hawkeye_quantize_prepare): the activation side of HawkeyeLinear.forward.
+
+    Returns (operand, scale [M, 1] fp32, q_fp8 [M, K] or None).  The scale and the staged
+    records are bit-identical to per_token_fp8 followed by HawkeyeOperand of its codes
+    (ref: __main__.py:148-154, then hawkeye.py:222-275 on the codes); the codes themselves
+    are written only when `codes` is set.
+    """
+    if x.device.type != "cuda":
+        raise RuntimeError("Hawkeye replay is CUDA-only")
+    rows = x.reshape(-1, x.shape[-1])
+    if rows.stride(-1) != 1:
+        rows = rows.contiguous()
+    m, k = int(rows.shape[0]), int(rows.shape[1])
+    dev = rows.device
+    lib = nat.lib()
+    op = HawkeyeOperand.__new__(HawkeyeOperand)
+    op.rows, op.k, op.device = m, k, dev
+    op.buffer = torch.empty((max(int(lib.ima_hawkeye_operand_bytes(m, k)), 16),), dtype=torch.uint8, device=dev)
+    op._source, op._version, op._data_ptr = None, None, 0   # an activation staging never matches a tensor
+    scale = torch.empty((m, 1), dtype=torch.float32, device=dev)
+    q = torch.empty((m, k), dtype=torch.uint8, device=dev) if codes else None
+    with torch.cuda.device(dev):
+        nat.call(
+            "ima_hawkeye_quantize_prepare", rows.data_ptr(), nat.dtype_code(rows.dtype), m, k,
+            rows.stride(0) if m > 1 else k, scale.data_ptr(), nat.ptr(q), k, op.buffer.data_ptr(),
+            nat.stream_of(dev),
+        )
+    return op, scale, (q.view(torch.float8_e4m3fn) if q is not None else None)
+
+
 def _validate_params(products_per_group: int, internal_width: int, zero_exponent: int) -> None:
     if products_per_group <= 0:
         raise ValueError("products_per_group must be positive")

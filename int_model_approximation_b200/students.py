@@ -21,7 +21,8 @@ import torch.nn as nn
 
 from . import _native as nat
 from .codebook import DigitPlanes, codebook_planes_from_fp8, int_gemm, per_token_fp8, planes_from_int32
-from .hawkeye import hawkeye_fp8_sum, stage_weight
+from .hawkeye import _validate_params as _validate_hawkeye_params
+from .hawkeye import hawkeye_replay, quantize_and_stage, stage_weight
 from .hawkeye_freivalds import exact_hawkeye_fp8_sum, stage_class_count_weight
 
 STUDENT_KERNEL = os.environ.get("IMA_STUDENT_KERNEL", "codebook")
@@ -276,18 +277,12 @@ class HawkeyeLinear(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _require_cuda_tensor(x, "Hawkeye input")
         in_shape = x.shape
-        x_fp8, x_scale = _per_token_fp8(x)
-        y, _stats = hawkeye_fp8_sum(
-            x_fp8,
-            x_scale,
-            self.weight,
-            self.weight_scale,
-            products_per_group=HAWKEYE_PRODUCTS_PER_GROUP,
-            internal_width=HAWKEYE_INTERNAL_WIDTH,
-            zero_exponent=HAWKEYE_ZERO_EXPONENT,
-            block_m=HAWKEYE_BLOCK_M,
-            block_n=HAWKEYE_BLOCK_N,
-        )
+        # the reference's _fp8_per_token then hawkeye_fp8_sum (__main__.py:467-481), with the
+        # quantisation and the activation staging fused into one launch, then the replay;
+        # the replay parameters are validated as hawkeye_fp8_sum validates them
+        _validate_hawkeye_params(HAWKEYE_PRODUCTS_PER_GROUP, HAWKEYE_INTERNAL_WIDTH, HAWKEYE_ZERO_EXPONENT)
+        x_op, x_scale, _ = quantize_and_stage(x)
+        y = hawkeye_replay(x_op, stage_weight(self.weight), x_scale, self.weight_scale)
         if self.bias is not None:
             y = y + self.bias.to(y.dtype)
         return y.to(x.dtype).reshape(*in_shape[:-1], self.out_features)

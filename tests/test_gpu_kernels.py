@@ -764,3 +764,43 @@ def test_grouped_gemm_many_problems_fp32_outputs(cuda_device):
         assert torch.equal(c.cpu(), c_ref)
         assert torch.equal(y.cpu().to(torch.float32).view(torch.int32), y_ref.to(y.dtype).to(torch.float32).view(torch.int32))
     _assert_status_clean(cuda_device)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("m,k", [(1, 1), (12, 903), (33, 64), (130, 257), (300, 896)])
+def test_fused_quantise_and_stage_equals_two_launches(cuda_device, dtype, m, k):
+    """ima_hawkeye_quantize_prepare writes the same scale, codes and staged operand bytes as
+    ima_quantize_per_token followed by ima_hawkeye_prepare, including rows with NaN, +-inf,
+    all zeros and subnormal values, a ragged K, padding rows up to the operand pitch and a
+    row stride wider than K."""
+    x = synthetic.student_t_activations(m, k + 5, seed=41 + m + k, outlier_fraction=0.02, dtype=torch.float32)
+    if m >= 8:
+        x[1, k // 2] = float("nan")
+        x[2, 0] = float("inf")
+        x[3, k - 1] = float("-inf")
+        x[4] = 0.0
+        x[5] = x[5] * 1e-38
+    xd = x.to(dtype).to(cuda_device)[:, :k]            # row stride k + 5
+    q_ref, s_ref, *_ = codebook.per_token_fp8(xd)
+    ref_op = hawkeye.HawkeyeOperand(q_ref)
+    op, scale, q = hawkeye.quantize_and_stage(xd, codes=True)
+    torch.cuda.synchronize()
+    assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8))
+    assert torch.equal(scale.view(torch.int32), s_ref.view(torch.int32))
+    assert torch.equal(op.buffer, ref_op.buffer)
+    op2, scale2, none = hawkeye.quantize_and_stage(xd)
+    assert none is None and torch.equal(op2.buffer, ref_op.buffer) and torch.equal(scale2, scale)
+
+
+def test_hawkeye_linear_forward_uses_the_fused_staging(cuda_device):
+    """HawkeyeLinear.forward (fused quantise + stage, then the replay) equals the reference
+    composition _fp8_per_token -> hawkeye_fp8_sum on 3-D input with a bias."""
+    w, ws = synthetic.normal_fp8_weights(70, 300, seed=77)
+    bias = torch.randn(70, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    lin = students.HawkeyeLinear(w.to(cuda_device), ws.to(cuda_device), bias.to(cuda_device))
+    x = synthetic.student_t_activations(2 * 19, 300, seed=5, outlier_fraction=0.02).reshape(2, 19, 300).to(cuda_device)
+    y = lin(x)
+    xq, xsc, *_ = codebook.per_token_fp8(x)
+    ref, _ = hawkeye.hawkeye_fp8_sum(xq, xsc, w.to(cuda_device), ws.to(cuda_device))
+    ref = (ref + bias.to(cuda_device).to(ref.dtype)).to(x.dtype).reshape(2, 19, 70)
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
