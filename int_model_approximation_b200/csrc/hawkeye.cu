@@ -76,16 +76,18 @@ __global__ void hawkeye_prepare_kernel(const uint8_t* __restrict__ src, int64_t 
 }
 
 // ---------------------------------------------------------------------------
-// Replay kernel.  CTA tile 128 x 128 outputs, 512 threads as a 32 x 16 grid;
-// thread (ty, tx) owns rows 4 ty + i (i < 4) and columns 2 tx + 32 jj + h
-// (jj < 4, h < 2), so each k step reads its operand records with two (A) and four
-// (B) 16-byte shared loads.  Records of group g + 1 stream in by cp.async while group
+// Replay kernel.  CTA tile 128 x 128 outputs on 512 threads; the thread of lane l in
+// warp w owns rows r0 + i (i < 4, r0 = 32 (w & 3) + 8 (w >> 2) + 4 (l >> 4)) and
+// columns 2 tx + 32 jj + h (tx = l & 15, jj < 4, h < 2), so each k step reads its
+// operand records with two (A) and four (B) 16-byte shared loads, and the rows of a
+// warp lie in the tensor-memory lane quadrant w & 3.  Records of group g + 1 stream in by cp.async while group
 // g is replayed (two stages, one barrier per group).  The power tiles travel by bulk
 // copies two groups ahead (three stages); thread 0 issues the MMAs of group g + 1
 // into one of two tensor-memory buffers while group g is replayed, so the maxima of a
 // group are ready when the group starts.  Each warp then reads a 32 x 32 block of
-// the maxima from tensor memory and writes them as bytes into a shared array laid out
-// by the owning thread's outputs (one 8-byte load per row of its tile).
+// the maxima from its lane quadrant and writes them as bytes into a shared array laid
+// out by the owning thread's outputs (one 8-byte load per row of its tile); the four
+// warps of a quadrant exchange them behind a 128-thread named barrier.
 //
 // Per output and group the accumulator is folded into the running sum before the
 // product loop (its aligned value, the bits(M_S) offsets and the sign corrections
@@ -212,7 +214,9 @@ hawkeye_replay_kernel(const uint2* __restrict__ recA, const unsigned char* __res
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + HK_OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + HK_OFF_MISC + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tx = tid & 15, ty = tid >> 4;
+    // rows of this thread: r0 + i; warp w's eight rows lie in tensor-memory lane quadrant w & 3
+    const int tx = tid & 15;
+    const int r0 = 32 * (warp & 3) + 8 * (warp >> 2) + 4 * (lane >> 4);
     const int64_t m0 = (int64_t)blockIdx.y * HK_BM;
     const int64_t n0 = (int64_t)blockIdx.x * HK_BN;
 
@@ -289,6 +293,7 @@ hawkeye_replay_kernel(const uint2* __restrict__ recA, const unsigned char* __res
     for (; g < groups; ++g) {
         hk_cp_async_wait_all();
         __syncthreads();   // records of g visible; every thread is done with group g - 1
+        if (*abort_flag) break;   // a wait of the previous group gave up
         if (tid == 0) {
             tc_fence_after();
             if (g + 2 < groups) {
@@ -332,13 +337,13 @@ hawkeye_replay_kernel(const uint2* __restrict__ recA, const unsigned char* __res
                 *reinterpret_cast<uint16_t*>(erow + (2 * c4 + 1) * 8) = (uint16_t)(w >> 16);
             }
         }
-        tc_fence_before();
-        __syncthreads();   // maxima of group g complete
-        if (*abort_flag) break;
+        tc_fence_before();   // tensor-memory reads ordered before the next group's MMAs
+        // the four warps of lane quadrant q wrote the maxima of its 32 rows, and read them
+        named_barrier_sync(1u + (uint32_t)(warp & 3), 128u);
 
 
         const unsigned char* s = sm + HK_OFF_REC + (g & 1) * HK_STAGE;
-        const uint2* sRecA = reinterpret_cast<const uint2*>(s) + ty * TM;
+        const uint2* sRecA = reinterpret_cast<const uint2*>(s) + r0;
         const uint2* sRecB = reinterpret_cast<const uint2*>(s + HK_OFF_RECB) + 2 * tx;
 
         // ---- per output: M_S and the folded start value of the sum ----
@@ -349,7 +354,7 @@ hawkeye_replay_kernel(const uint2* __restrict__ recA, const unsigned char* __res
         // added up front.
         uint32_t mb[TM][TN], sum[TM][TN];
         {
-            const uint4 sa4 = *reinterpret_cast<const uint4*>(s + HK_OFF_SGA + ty * TM * 4);
+            const uint4 sa4 = *reinterpret_cast<const uint4*>(s + HK_OFF_SGA + r0 * 4);
             const uint32_t sav[4] = {sa4.x, sa4.y, sa4.z, sa4.w};
             uint32_t sbv[TN];
 #pragma unroll
@@ -358,7 +363,7 @@ hawkeye_replay_kernel(const uint2* __restrict__ recA, const unsigned char* __res
                 sbv[2 * jj] = t.x;
                 sbv[2 * jj + 1] = t.y;
             }
-            const unsigned char* erow = sm + HK_OFF_E + (ty * TM) * HK_E_PITCH + tx * 8;
+            const unsigned char* erow = sm + HK_OFF_E + r0 * HK_E_PITCH + tx * 8;
 #pragma unroll
             for (int i = 0; i < TM; ++i) {
                 const uint2 eu = *reinterpret_cast<const uint2*>(erow + i * HK_E_PITCH);
@@ -417,7 +422,9 @@ hawkeye_replay_kernel(const uint2* __restrict__ recA, const unsigned char* __res
 
     // ---- after a timeout: wait (bounded) for the copies and MMAs still in flight ----
     hk_cp_async_wait_all();
-    if (g < groups && tid == 0) {
+    __syncthreads();
+    const bool aborted = *abort_flag != 0;
+    if (aborted && tid == 0) {
         constexpr uint64_t DRAIN_NS = 100000000ull;
         for (int64_t pg = mma_issued; pg < pow_issued; ++pg)
             hk_drain_wait(&pow_full[pg % HK_POW_STAGES], (uint32_t)((pg / HK_POW_STAGES) & 1), DRAIN_NS);
@@ -430,12 +437,12 @@ hawkeye_replay_kernel(const uint2* __restrict__ recA, const unsigned char* __res
         tc_fence_after();
         tmem_dealloc(tmem, HK_TMEM_COLS);
     }
-    if (g < groups) return;   // timed out: the device status word holds IMA_ERR_TIMEOUT
+    if (aborted) return;   // timed out: the device status word holds IMA_ERR_TIMEOUT
 
     // ---- epilogue: gfloat = acc * 2^-20; y = (gfloat * xs) * ws; bf16 RNE ----
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
-        int64_t m = m0 + ty * TM + i;
+        int64_t m = m0 + r0 + i;
         if (m >= M) continue;
         float xs = x_scale[m];
 #pragma unroll
