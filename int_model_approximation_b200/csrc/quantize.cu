@@ -367,18 +367,17 @@ __global__ void __launch_bounds__(256, 3) quantize_rows_kernel(const __grid_cons
 // Per-token quantisation fused with the Hawkeye operand staging (ima_hawkeye_quantize_prepare):
 // the row scale and the e4m3 codes exactly as quantize_rows_kernel computes them (the same
 // amax, scale, division and cast functions), written straight into the [k][row] records the
-// replay reads (the layout of hawkeye_layout.cuh: per k the record {|s| 2^e as fp32 bits, sign
+// replay reads (the blocks of hawkeye_layout.cuh: per k the record {|s| 2^e as fp32 bits, sign
 // mask}, per group the exponent powers and the sign word), and optionally the codes.
 // A block covers 32 rows.  Phase 1: 8 warps x 4 rows, the NaN-propagating amax and the scale.
 // Phase 2: thread (row = lane, warp) takes groups warp, warp + 8, ...: 32 elements -> 32 codes
-// -> records; for each k the block's 32 rows form one contiguous 256-byte store.
+// -> records; for each k the 32 rows of a thread block form one contiguous 256-byte store.
 constexpr int HQ_GROUP = HK_GROUP;
 
 __global__ void __launch_bounds__(256) hawkeye_quant_stage_kernel(const void* __restrict__ x, int dtype, int64_t M,
                                                                   int64_t K, int64_t ldx, float* __restrict__ scale,
                                                                   uint8_t* __restrict__ q, int64_t ldq, int64_t pitch,
-                                                                  int64_t groups, uint2* __restrict__ rec,
-                                                                  unsigned char* __restrict__ pow, uint32_t* __restrict__ sg) {
+                                                                  int64_t groups, unsigned char* __restrict__ op) {
     __shared__ float s_s[32], s_y[32];
     __shared__ int s_mode[32];   // 1: fast path (finite scale, half input); 2: IEEE, finite scale; 0: IEEE, NaN/inf
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -473,6 +472,7 @@ __global__ void __launch_bounds__(256) hawkeye_quant_stage_kernel(const void* __
         }
         // the replay's operand records, element by element as ima_hawkeye_prepare writes them
         uint32_t signs = 0, pw[16];
+        uint2 rec[HQ_GROUP];
 #pragma unroll
         for (int j = 0; j < HQ_GROUP; ++j) {
             const int64_t k = g * HQ_GROUP + j;
@@ -484,13 +484,12 @@ __global__ void __launch_bounds__(256) hawkeye_quant_stage_kernel(const void* __
             const float mag = valid ? (float)sig * (float)(1u << e) : 0.0f;
             const uint32_t mask = (valid && (b & 0x80u)) ? 0xFFFFFFFFu : 0u;
             signs |= (mask & 1u) << j;
-            rec[(g * HQ_GROUP + j) * pitch + m] = make_uint2(__float_as_uint(mag), mask);
+            rec[j] = make_uint2(__float_as_uint(mag), mask);
             const uint32_t p = hk_pow_bits(valid && sig != 0, e);
             if (j & 1) pw[j >> 1] |= p << 16;
             else pw[j >> 1] = p;
         }
-        hk_store_pow(pow, g, m, pitch, pw);
-        sg[g * pitch + m] = signs;
+        hk_store_row(op, g, m, pitch, rec, pw, signs);
     }
 }
 
@@ -683,11 +682,8 @@ int ima_hawkeye_quantize_prepare(const void* x, int x_dtype, int64_t M, int64_t 
     const int64_t pitch = ima_hawkeye_operand_pitch(M), groups = (K + HQ_GROUP - 1) / HQ_GROUP;
     if (pitch == 0 || groups == 0) return IMA_OK;
     if (pitch / 32 > INT32_MAX) return IMA_ERR_UNSUPPORTED;
-    uint2* rec = reinterpret_cast<uint2*>(operand);
-    unsigned char* pow = reinterpret_cast<unsigned char*>(rec + pitch * groups * HQ_GROUP);
-    uint32_t* sg = reinterpret_cast<uint32_t*>(pow + pitch * groups * 64);
     hawkeye_quant_stage_kernel<<<(unsigned)(pitch / 32), 256, 0, (cudaStream_t)stream>>>(
-        x, x_dtype, M, K, ldx, scale, q_fp8, ldq, pitch, groups, rec, pow, sg);
+        x, x_dtype, M, K, ldx, scale, q_fp8, ldq, pitch, groups, reinterpret_cast<unsigned char*>(operand));
     return IMA_LAUNCH_STATUS();
 }
 
