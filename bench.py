@@ -709,7 +709,7 @@ def run_c1(args) -> dict:
                 "exact_int_ops_per_step_per_gpu": flops,
                 "l2": "inputs larger than L2 (about 2.4 GB of weight planes and activations per step)",
                 "launch": "three CUDA graphs per step on one stream: grouped quantiser, grouped GEMM (up to "
-                          "80 linears per launch), Freivalds row check of every product (one launch)",
+                          "64 linears per launch), Freivalds row check of every product (one launch)",
                 "parallelism": f"replicas x{world} (token batches per rank)",
             },
             "freivalds_mismatch_rows": mismatches,
@@ -997,9 +997,10 @@ def run_headline(args) -> None:
     north star says: token rows over the ranks with the weights replicated, gate/up split by
     output columns (every rank holds all tokens for them), and the bf16 outputs gathered to
     every rank.  A step is one forward of all 196 linears: per layer the grouped quantiser,
-    the exact int64 GEMM with the fused rescale (one grouped launch), the gathers of its
-    outputs (peer-to-peer copies on the copy engines, started as soon as the GEMM has written
-    them) and the Freivalds row check of every local int64 product.  Strong scaling: the
+    the exact int64 GEMM with the fused rescale (one grouped launch) whose epilogue also stores
+    every bf16 output into every rank's gathered buffer over NVLink (`--c4-gather ce`: peer-to-
+    peer copies on the copy engines after the GEMM instead), and the Freivalds row check of
+    every local int64 product.  Strong scaling: the
     16384 tokens are fixed.  value = exact int ops of the whole model / step time (max over
     ranks).  At N = 1 the line also carries config 1 (the 0.5B codebook stack), config 2
     (Hawkeye replay) and config 3 (class counts); at every N it carries config 4's Hawkeye
@@ -1086,12 +1087,24 @@ def run_headline(args) -> None:
             peer_sent.append([None if q == rank else torch.cuda.Event.from_ipc_handle(device, everyone[q][1][s])
                               for s in range(2)])
 
+    fused = world > 1 and args.c4_gather == "epilogue"
+    if fused:
+        # the GEMM epilogue stores every output chunk into every rank's gathered buffer
+        for layer in range(layers):
+            for s in range(2):
+                views[layer][s]["y_copies"] = [
+                    [peer_bufs[dst][s * len(specs) + p] + rank * sp["rows"] * sp["n"] * 2 for dst in range(world)]
+                    for p, sp in enumerate(specs)]
+
     def gather(s: int) -> None:
         """Copies of this rank's output shards of buffer set s into every rank's gathered
-        buffers (ordered after the GEMM that wrote them)."""
+        buffers (ordered after the GEMM that wrote them); with the fused gather the GEMM has
+        written them already, and only the completion events are recorded."""
         computed[s].record(cs)
-        if world == 1:
+        if world == 1 or fused:
             drained[s].record(cs)
+            if fused:
+                sent[s].record(cs)
             return
         for q in range(world):
             dst = (rank + q) % world                  # start at different peers on different ranks
@@ -1185,6 +1198,27 @@ def run_headline(args) -> None:
     if world > 1:
         dist.all_reduce(gt, op=dist.ReduceOp.MAX)
     gemm_ms = float(gt.item())
+    gather_check = None
+    if world > 1:
+        # every rank's gathered buffers hold, for each buffer set, the outputs of the last layer
+        # that used it on every rank: compare them with an NCCL all-gather of the local outputs
+        ok, nbytes = True, 0
+        with torch.cuda.stream(cs):
+            for s in range(2):
+                for p, sp in enumerate(specs):
+                    shard = sp["rows"] * sp["n"]
+                    mine = torch.empty((world * shard,), dtype=torch.bfloat16, device=device)
+                    nat.call("ima_copy_async", mine.data_ptr(), own_bufs[s * len(specs) + p], world * shard * 2,
+                             cs.cuda_stream)
+                    ref = torch.empty_like(mine)
+                    dist.all_gather_into_tensor(ref, sets[s]["y"][p].reshape(-1).contiguous())
+                    ok = ok and bool(torch.equal(mine.view(torch.int16), ref.view(torch.int16)))
+                    nbytes += world * shard * 2
+        flag = torch.tensor([0 if ok else 1], dtype=torch.int32, device=device)
+        dist.all_reduce(flag)
+        gather_check = {"ok": int(flag.item()) == 0, "bytes_checked_per_gpu": nbytes,
+                        "what": "each GPU's gathered buffers of both buffer sets vs an NCCL all-gather of the "
+                                "ranks' local outputs, bit for bit"}
 
     # ---- end to end through the public API: host inputs in, the step's result out ----
     host_x = [x.cpu().pin_memory() for x in xs]
@@ -1236,14 +1270,19 @@ def run_headline(args) -> None:
             "tokens": tokens,
             "exact_int_ops_per_step": ops,
             "parallelism": f"token rows over {world} GPU(s), gate/up output columns over {world} GPU(s)",
-            "gather": ("copy engines: peer-to-peer copies into CUDA-IPC-shared buffers, receiver-side completion by "
-                       "interprocess events" if world > 1 else None),
+            "gather": (None if world == 1 else
+                       "fused into the GEMM epilogue: every output chunk stored into every GPU's gathered buffer "
+                       "(CUDA-IPC peer memory, plain NVLink stores), receiver-side completion by interprocess "
+                       "events" if fused else
+                       "copy engines: peer-to-peer copies into CUDA-IPC-shared buffers, receiver-side completion by "
+                       "interprocess events"),
             "nvlink_bytes_received_per_gpu_per_step": gather_bytes,
             "l2": "inputs larger than L2 (2.3 GB of weight digit planes per layer)",
             "activations": "the seven activation matrices of a layer are shared by the 28 layers (the work per "
                            "layer is unchanged)",
         },
         "freivalds_mismatch_rows": int(bad.item()),
+        "gather_check": gather_check,
         "gpu_launches": sum(st.launches_per_forward() for st in stacks) * args.steps,
         "roofline": {
             "kernel": "int_gemm_kernel<DIGITS3>",
@@ -1483,6 +1522,8 @@ def main() -> None:
     ap.add_argument("--c4-tokens", type=int, default=16384)
     ap.add_argument("--c4-layers", type=int, default=28)
     ap.add_argument("--c4-hawkeye-steps", type=int, default=1)
+    ap.add_argument("--c4-gather", choices=["epilogue", "ce"], default="epilogue",
+                    help="N > 1: gather the outputs from the GEMM epilogue (default) or by copy-engine copies")
     ap.add_argument("--c1-only", action="store_true", help="only the config-1 measurement (one GPU)")
     ap.add_argument("--profile-c4", action="store_true", help="two eager forwards of --c4-layers layers (for ncu)")
     args = ap.parse_args()

@@ -154,7 +154,7 @@ int ima_int_gemm(const int8_t* a_planes, int64_t lda, const int8_t* b_planes, in
                  int64_t K, int scheme, int64_t* c, int64_t ldc, const float* x_scale, const float* w_scale,
                  const float* bias, void* y, int y_dtype, int64_t ldy, void* stream);
 
-/* Many independent products in as few launches as possible (one per 80 problems): every
+/* Many independent products in as few launches as possible (one per 64 problems): every
  * linear of a model in one call.  Fields mean what the arguments of ima_int_gemm mean;
  * all problems use the same digit scheme. */
 typedef struct ima_gemm_problem {
@@ -173,6 +173,21 @@ typedef struct ima_gemm_problem {
     int64_t ldy;
 } ima_gemm_problem;
 int ima_int_gemm_grouped(const ima_gemm_problem* problems, int count, int scheme, void* stream);
+/* The same GEMMs, with each problem's y written to up to 8 further destinations besides
+ * problems[i].y, all with y's layout (row stride ldy, dtype y_dtype): copies[i].y[d], NULL
+ * entries skipped.  For a multi-GPU caller these are the other GPUs' gathered-output
+ * buffers (peer memory opened through CUDA IPC, or local memory): the epilogue stores each
+ * output chunk to every destination, so the gather of the outputs rides on the GEMM itself
+ * (plain stores over NVLink, no copy engines, no collective launch) and is complete when
+ * the launch is.  copies == NULL is ima_int_gemm_grouped.  A problem without y must have no
+ * copies (IMA_ERR_INVALID_ARGUMENT).  No reference counterpart: the reference runs on one
+ * GPU (__main__.py:115-126). */
+#define IMA_GEMM_MAX_Y_COPIES 8
+typedef struct ima_gemm_y_copies {
+    void* y[IMA_GEMM_MAX_Y_COPIES];
+} ima_gemm_y_copies;
+int ima_int_gemm_grouped_copies(const ima_gemm_problem* problems, const ima_gemm_y_copies* copies, int count,
+                                int scheme, void* stream);
 /* Process-wide cap on the number of persistent GEMM CTAs (one per SM); 0 (the default)
  * uses every SM.  A multi-GPU caller leaves a few SMs to the collectives it overlaps with
  * the GEMM (a persistent CTA never yields its SM, so a collective kernel queued behind a

@@ -59,6 +59,12 @@ class GemmProblem(ctypes.Structure):
     ]
 
 
+class GemmYCopies(ctypes.Structure):
+    """ima_gemm_y_copies"""
+
+    _fields_ = [("y", _VP * 8)]
+
+
 class FreivaldsRowsProblem(ctypes.Structure):
     """ima_freivalds_rows_problem"""
 
@@ -76,6 +82,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ima_quant_fast_selftest": (_I32, [_I32, _VP, _VP]),
     "ima_quantize_grouped": (_I32, [_VP, _I32, _VP]),
     "ima_int_gemm_grouped": (_I32, [_VP, _I32, _I32, _VP]),
+    "ima_int_gemm_grouped_copies": (_I32, [_VP, _VP, _I32, _I32, _VP]),
     "ima_set_gemm_sm_limit": (_I32, [_I32]),
     "ima_set_gemm_wait_test": (_I32, [_I64]),
     "ima_ipc_handle_bytes": (_I32, []),

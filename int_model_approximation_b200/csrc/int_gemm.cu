@@ -51,7 +51,8 @@ constexpr int GM_KT = 64;                  // bytes of K per stage (one 64-byte 
 constexpr int GM_EPI_WARPS = 8;            // two per TMEM lane quadrant
 constexpr int GM_THREADS = 64 + GM_EPI_WARPS * 32;
 constexpr uint32_t GM_TMEM_COLS = 512;
-constexpr int GM_MAXP = 80;                // problems per launch (kernel-parameter budget)
+constexpr int GM_MAXP = 64;                // problems per launch (kernel-parameter budget)
+constexpr int GM_MAXD = 8;                 // extra destinations of y per problem (ima_int_gemm_grouped_copies)
 
 template <int SCHEME>
 struct Scheme;
@@ -108,16 +109,21 @@ struct GemmProblemDev {
     const float* bias;
     int64_t ldc, ldy;
     int32_t M, N, K, y_dtype;
-    int32_t m_tiles, k_tiles, vec_out, pad;
+    int32_t m_tiles, k_tiles, vec_out, ncopy;   // ncopy: extra destinations of y (batch.ycopy)
 };
 
 struct __align__(64) GemmBatch {
     CUtensorMap maps[GM_MAXP][2];   // A planes, B planes
     GemmProblemDev p[GM_MAXP];
+    void* ycopy[GM_MAXP][GM_MAXD];  // further copies of each problem's y (same layout, ldy)
     int32_t tile_start[GM_MAXP + 1];
     int32_t n;
+    int32_t has_copies;             // some problem writes copies of y
     uint64_t stall_ns;              // test knob (ima_set_gemm_wait_test); 0 in normal use
 };
+
+static_assert(sizeof(GemmBatch) <= 32764, "kernel parameters of one grouped GEMM launch");
+static_assert(GM_MAXD == IMA_GEMM_MAX_Y_COPIES, "copies per problem");
 
 IMA_DEVINL int find_problem(const GemmBatch& b, int64_t t) {
     int lo = 0, hi = b.n - 1;
@@ -414,19 +420,26 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                             const int64_t gn = cbase + part * (16 / esize);
                             const uint4 v = *reinterpret_cast<const uint4*>(yst + r * row_bytes + part * 16);
                             if (gm < P.M && gn < P.N) {
-                                unsigned char* dst = reinterpret_cast<unsigned char*>(P.y) + (gm * P.ldy + gn) * esize;
+                                const int64_t off = (gm * P.ldy + gn) * esize;
                                 const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-                                if (gn + 16 / esize <= P.N) {
-                                    *reinterpret_cast<uint4*>(dst) = v;
-                                } else if (esize == 4) {
+                                // y, then each further copy of it (another GPU's gathered
+                                // buffer: plain stores over NVLink)
+                                for (int d = -1; d < P.ncopy; ++d) {
+                                    unsigned char* dst =
+                                        reinterpret_cast<unsigned char*>(d < 0 ? P.y : batch.ycopy[pi][d]) + off;
+                                    if (gn + 16 / esize <= P.N) {
+                                        *reinterpret_cast<uint4*>(dst) = v;
+                                    } else if (esize == 4) {
 #pragma unroll
-                                    for (int e = 0; e < 4; ++e)
-                                        if (gn + e < P.N) reinterpret_cast<uint32_t*>(dst)[e] = w4[e];
-                                } else {
+                                        for (int e = 0; e < 4; ++e)
+                                            if (gn + e < P.N) reinterpret_cast<uint32_t*>(dst)[e] = w4[e];
+                                    } else {
 #pragma unroll
-                                    for (int e = 0; e < 8; ++e)
-                                        if (gn + e < P.N)
-                                            reinterpret_cast<uint16_t*>(dst)[e] = (uint16_t)(w4[e >> 1] >> (16 * (e & 1)));
+                                        for (int e = 0; e < 8; ++e)
+                                            if (gn + e < P.N)
+                                                reinterpret_cast<uint16_t*>(dst)[e] =
+                                                    (uint16_t)(w4[e >> 1] >> (16 * (e & 1)));
+                                    }
                                 }
                             }
                         }
@@ -438,18 +451,23 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                         if (n >= P.N) break;
                         if (P.c) P.c[m * P.ldc + n] = (int64_t)cval[j];
                         if (P.y) {
-                            if (P.y_dtype == IMA_DTYPE_F32)
-                                reinterpret_cast<float*>(P.y)[m * P.ldy + n] = yv[j];
-                            else if (P.y_dtype == IMA_DTYPE_BF16)
-                                reinterpret_cast<__nv_bfloat16*>(P.y)[m * P.ldy + n] = __float2bfloat16_rn(yv[j]);
-                            else
-                                reinterpret_cast<__half*>(P.y)[m * P.ldy + n] = __float2half_rn(yv[j]);
+                            for (int d = -1; d < P.ncopy; ++d) {
+                                void* yd = d < 0 ? P.y : batch.ycopy[pi][d];
+                                if (P.y_dtype == IMA_DTYPE_F32)
+                                    reinterpret_cast<float*>(yd)[m * P.ldy + n] = yv[j];
+                                else if (P.y_dtype == IMA_DTYPE_BF16)
+                                    reinterpret_cast<__nv_bfloat16*>(yd)[m * P.ldy + n] = __float2bfloat16_rn(yv[j]);
+                                else
+                                    reinterpret_cast<__half*>(yd)[m * P.ldy + n] = __float2half_rn(yv[j]);
+                            }
                         }
                     }
                 }
             }
         }
     }
+    // copies of y written into other GPUs' memory are visible there once the launch is complete
+    if (batch.has_copies) __threadfence_system();
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
@@ -539,7 +557,7 @@ int launch_batch(GemmBatch& b, cudaStream_t stream) {
 }
 
 template <int SCHEME>
-int run_grouped(const ima_gemm_problem* problems, int count, cudaStream_t stream) {
+int run_grouped(const ima_gemm_problem* problems, const ima_gemm_y_copies* copies, int count, cudaStream_t stream) {
     using L = GemmCfg<SCHEME>;
     struct Item { int idx; int64_t cost; };
     std::vector<Item> items;
@@ -584,6 +602,16 @@ int run_grouped(const ima_gemm_problem* problems, int count, cudaStream_t stream
             bool vec = true;
             if (q.c) vec = vec && !(reinterpret_cast<uintptr_t>(q.c) & 15) && !((q.ldc * 8) & 15);
             if (q.y) vec = vec && !(reinterpret_cast<uintptr_t>(q.y) & 15) && !((q.ldy * yes) & 15);
+            D.ncopy = 0;
+            if (copies && q.y) {
+                for (int d = 0; d < GM_MAXD; ++d) {
+                    void* yc = copies[idx].y[d];
+                    if (!yc) continue;
+                    vec = vec && !(reinterpret_cast<uintptr_t>(yc) & 15);
+                    b.ycopy[k][D.ncopy++] = yc;
+                }
+                if (D.ncopy) b.has_copies = 1;
+            }
             D.vec_out = vec ? 1 : 0;
             b.tile_start[k] = tiles;
             tiles += D.m_tiles * (int32_t)((q.N + L::BN - 1) / L::BN);
@@ -611,16 +639,25 @@ extern "C" int ima_set_gemm_sm_limit(int sms) {
     return IMA_OK;
 }
 
-extern "C" int ima_int_gemm_grouped(const ima_gemm_problem* problems, int count, int scheme, void* stream) {
+extern "C" int ima_int_gemm_grouped_copies(const ima_gemm_problem* problems, const ima_gemm_y_copies* copies,
+                                           int count, int scheme, void* stream) {
     if (count < 0 || (count > 0 && !problems)) return IMA_ERR_INVALID_ARGUMENT;
     if (scheme != IMA_SCHEME_DIGITS3 && scheme != IMA_SCHEME_DIGITS5) return IMA_ERR_UNSUPPORTED;
     for (int i = 0; i < count; ++i) {
         int rc = check_problem(problems[i], scheme);
         if (rc != IMA_OK) return rc;
+        if (copies && !problems[i].y) {
+            for (int d = 0; d < GM_MAXD; ++d)
+                if (copies[i].y[d]) return IMA_ERR_INVALID_ARGUMENT;   // copies of a y that is not written
+        }
     }
     if (scheme == IMA_SCHEME_DIGITS3)
-        return run_grouped<IMA_SCHEME_DIGITS3>(problems, count, (cudaStream_t)stream);
-    return run_grouped<IMA_SCHEME_DIGITS5>(problems, count, (cudaStream_t)stream);
+        return run_grouped<IMA_SCHEME_DIGITS3>(problems, copies, count, (cudaStream_t)stream);
+    return run_grouped<IMA_SCHEME_DIGITS5>(problems, copies, count, (cudaStream_t)stream);
+}
+
+extern "C" int ima_int_gemm_grouped(const ima_gemm_problem* problems, int count, int scheme, void* stream) {
+    return ima_int_gemm_grouped_copies(problems, nullptr, count, scheme, stream);
 }
 
 extern "C" int ima_int_gemm(const int8_t* a_planes, int64_t lda, const int8_t* b_planes, int64_t ldb, int64_t M,

@@ -5,7 +5,7 @@
 weight half of the check t = codebook(W)^T r, both fixed) and runs one forward of all
 of them -- per-token quantisation, the exact int64 GEMM with the fused
 rescale/bias/bf16 epilogue, and the Freivalds row check of every int64 product -- as
-grouped launches (one quantiser launch, one GEMM launch per 80 linears, one Freivalds
+grouped launches (one quantiser launch, one GEMM launch per 64 linears, one Freivalds
 launch for all products), entirely on the device and without host synchronisation.  The
 three phases can be run (and captured into CUDA graphs) separately or together.
 
@@ -39,7 +39,7 @@ class PreparedLinear:
 
 
 class CodebookStack:
-    GEMM_BATCH = 80    # problems per GEMM launch (kernel-parameter budget of the C side)
+    GEMM_BATCH = 64    # problems per GEMM launch (kernel-parameter budget of the C side)
     CHECK_BATCH = 192  # products per Freivalds row-pass launch (kernel-parameter budget of the C side)
 
     def __init__(self, weights: list[tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]], *, seed: int = 0):
@@ -103,10 +103,20 @@ class CodebookStack:
             f.c, f.ldc, f.r = bufs["c"][i].data_ptr(), lin.n, lin.r.data_ptr()
             f.M, f.N, f.K, f.a_kind = m, lin.n, lin.k, nat.IMA_FREIVALDS_A_FP8
             f.mismatch_rows = bufs["mismatch"].data_ptr()
+        copies = bufs.get("y_copies")
         gemm_batches = []
         for members in self._batches():
             g_arr = (nat.GemmProblem * len(members))(*[gemm[i] for i in members])
-            gemm_batches.append((g_arr, len(members)))
+            c_arr = None
+            if copies:
+                c_arr = (nat.GemmYCopies * len(members))()
+                for slot, i in enumerate(members):
+                    dests = list(copies[i])
+                    if len(dests) > 8:
+                        raise ValueError("at most 8 further copies of a linear's output")
+                    for d, ptr in enumerate(dests):
+                        c_arr[slot].y[d] = ptr
+            gemm_batches.append((g_arr, len(members), c_arr))
         return quant, gemm_batches, rows
 
     def _prepared(self, xs: list[torch.Tensor], bufs: dict) -> tuple:
@@ -140,12 +150,21 @@ class CodebookStack:
 
     def multiply(self, xs: list[torch.Tensor], bufs: dict) -> None:
         """The exact int64 GEMM with the fused rescale/bias/bf16 epilogue of every linear
-        (reads the planes that quantize() wrote): a few cost-balanced grouped launches."""
+        (reads the planes that quantize() wrote): a few cost-balanced grouped launches.
+
+        With bufs["y_copies"] (per linear, up to 8 device addresses with the layout of
+        bufs["y"][i], e.g. other GPUs' gathered-output buffers opened through CUDA IPC) the
+        epilogue also stores every bf16 output to each of them: the gather of the outputs is
+        done when the launch is."""
         _q, gemm_batches, _f = self._prepared(xs, bufs)
         main = torch.cuda.current_stream(self.device)
-        for g_arr, count in gemm_batches:
-            nat.check("ima_int_gemm_grouped", nat.lib().ima_int_gemm_grouped(
-                ctypes.byref(g_arr), count, nat.IMA_SCHEME_DIGITS3, main.cuda_stream))
+        for g_arr, count, c_arr in gemm_batches:
+            if c_arr is None:
+                nat.check("ima_int_gemm_grouped", nat.lib().ima_int_gemm_grouped(
+                    ctypes.byref(g_arr), count, nat.IMA_SCHEME_DIGITS3, main.cuda_stream))
+            else:
+                nat.check("ima_int_gemm_grouped_copies", nat.lib().ima_int_gemm_grouped_copies(
+                    ctypes.byref(g_arr), ctypes.byref(c_arr), count, nat.IMA_SCHEME_DIGITS3, main.cuda_stream))
 
     def verify(self, xs: list[torch.Tensor], bufs: dict) -> None:
         """The Freivalds row check of every int64 product that multiply() wrote, failed rows

@@ -805,3 +805,59 @@ def test_hawkeye_linear_forward_uses_the_fused_staging(cuda_device):
     ref, _ = hawkeye.hawkeye_fp8_sum(xq, xsc, w.to(cuda_device), ws.to(cuda_device))
     ref = (ref + bias.to(cuda_device).to(ref.dtype)).to(x.dtype).reshape(2, 19, 70)
     assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+
+
+def test_grouped_gemm_writes_every_copy_of_y(cuda_device):
+    """ima_int_gemm_grouped_copies stores each problem's y into every further destination it
+    is given (here local buffers standing in for other GPUs' gathered buffers): 16-byte
+    aligned copies through the staged vector path, a copy at an odd element offset through
+    the element path, problems without copies unchanged; c and y equal the plain grouped
+    launch bit for bit, and the copies equal y."""
+    import ctypes
+
+    probs, copies, keep, outs = [], [], [], []
+    for i in range(5):
+        m, n, k = 40 + 70 * i, 24 + 56 * i, 64 + 200 * i
+        x = synthetic.student_t_activations(m, k, seed=70 + i)
+        w, ws = synthetic.normal_fp8_weights(n, k, seed=170 + i)
+        _q, _xs, _cb, cs, a = codebook.per_token_fp8(x.to(cuda_device), codebook=True, planes=True)
+        b, _ = codebook.codebook_planes_from_fp8(w.to(cuda_device))
+        wsc = (ws.reshape(-1) / 512.0).to(cuda_device)
+        c = torch.empty((m, n), dtype=torch.int64, device=cuda_device)
+        y = torch.empty((m, n), dtype=torch.bfloat16, device=cuda_device)
+        g = nat.GemmProblem()
+        g.a_planes, g.lda, g.b_planes, g.ldb = a.planes.data_ptr(), a.ld, b.planes.data_ptr(), b.ld
+        g.M, g.N, g.K, g.c, g.ldc = m, n, k, c.data_ptr(), n
+        g.x_scale, g.w_scale, g.bias = cs.reshape(-1).data_ptr(), wsc.data_ptr(), None
+        g.y, g.y_dtype, g.ldy = y.data_ptr(), nat.IMA_DTYPE_BF16, n
+        cp = nat.GemmYCopies()
+        dests = []
+        for d in range((0, 1, 2, 3, 8)[i]):
+            buf = torch.full((m * n + 8,), -1, dtype=torch.int16, device=cuda_device)
+            off = 1 if (i == 3 and d == 1) else 0           # odd element offset: not 16-byte aligned
+            cp.y[d] = buf.data_ptr() + 2 * off
+            dests.append((buf, off))
+        probs.append(g)
+        copies.append(cp)
+        keep += [a, b, cs, wsc]
+        outs.append((c, y, dests, m, n))
+    arr = (nat.GemmProblem * len(probs))(*probs)
+    carr = (nat.GemmYCopies * len(copies))(*copies)
+    lib = nat.lib()
+    nat.check("copies", lib.ima_int_gemm_grouped_copies(ctypes.byref(arr), ctypes.byref(carr), len(probs),
+                                                       nat.IMA_SCHEME_DIGITS3, nat.stream_of(cuda_device)))
+    torch.cuda.synchronize()
+    first = [(c.clone(), y.clone()) for c, y, _d, _m, _n in outs]
+    nat.check("plain", lib.ima_int_gemm_grouped(ctypes.byref(arr), len(probs), nat.IMA_SCHEME_DIGITS3,
+                                               nat.stream_of(cuda_device)))
+    torch.cuda.synchronize()
+    for (c0, y0), (c, y, dests, m, n) in zip(first, outs):
+        assert torch.equal(c0, c) and torch.equal(y0.view(torch.int16), y.view(torch.int16))
+        for buf, off in dests:
+            assert torch.equal(buf[off:off + m * n].view(m, n), y.view(torch.int16))
+            assert bool((buf[:off] == -1).all()) and bool((buf[off + m * n:] == -1).all())
+    _assert_status_clean(cuda_device)
+    # copies of a y that is not written are refused
+    arr[1].y = None
+    assert lib.ima_int_gemm_grouped_copies(ctypes.byref(arr), ctypes.byref(carr), len(probs),
+                                           nat.IMA_SCHEME_DIGITS3, nat.stream_of(cuda_device)) != 0
