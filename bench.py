@@ -997,10 +997,11 @@ def run_headline(args) -> None:
     north star says: token rows over the ranks with the weights replicated, gate/up split by
     output columns (every rank holds all tokens for them), and the bf16 outputs gathered to
     every rank.  A step is one forward of all 196 linears: per layer the grouped quantiser,
-    the exact int64 GEMM with the fused rescale (one grouped launch) whose epilogue also stores
-    every bf16 output into every rank's gathered buffer over NVLink (`--c4-gather ce`: peer-to-
-    peer copies on the copy engines after the GEMM instead), and the Freivalds row check of
-    every local int64 product.  Strong scaling: the
+    the exact int64 GEMM with the fused rescale (one grouped launch), the gathers of its
+    outputs (peer-to-peer copies on the copy engines, started as soon as the GEMM has written
+    them; `--c4-gather sm`: one copy kernel per layer on SMs kept from the GEMM; `--c4-gather
+    epilogue`: stores from the GEMM epilogue) and the Freivalds row check of every local
+    int64 product.  Strong scaling: the
     16384 tokens are fixed.  value = exact int ops of the whole model / step time (max over
     ranks).  At N = 1 the line also carries config 1 (the 0.5B codebook stack), config 2
     (Hawkeye replay) and config 3 (class counts); at every N it carries config 4's Hawkeye
@@ -1047,6 +1048,7 @@ def run_headline(args) -> None:
     views = [[dict(sets[s]) for s in range(2)] for _ in range(layers)]   # own descriptor caches per layer
     cs = torch.cuda.Stream(device)                    # compute
     ms = torch.cuda.Stream(device, priority=-1)       # gather bookkeeping
+    gs_copy = torch.cuda.Stream(device, priority=-1)  # copy kernels of the SM gather
     ce_streams = [torch.cuda.Stream(device, priority=-1) for _ in range(world)]   # one per destination rank
     ce_done = [[torch.cuda.Event() for _ in range(world)] for _ in range(2)]
     computed = [torch.cuda.Event(), torch.cuda.Event()]
@@ -1088,12 +1090,33 @@ def run_headline(args) -> None:
                               for s in range(2)])
 
     fused = world > 1 and args.c4_gather == "epilogue"
+    sm_gather = world > 1 and args.c4_gather == "sm"
+    copy_descs = []
+    if sm_gather:
+        # one copy launch per layer: every output shard to every rank's gathered buffer, the
+        # destinations in the order rank, rank + 1, ... (the ranks write to different GPUs)
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        nat.call("ima_set_gemm_sm_limit", max(1, sms - args.c4_gather_sms))
+        for s in range(2):
+            descs = (nat.CopyDesc * (world * len(specs)))()
+            i = 0
+            for q in range(world):
+                for p, sp in enumerate(specs):
+                    shard = sp["rows"] * sp["n"] * 2
+                    descs[i].dst = peer_bufs[(rank + q) % world][s * len(specs) + p] + rank * shard
+                    descs[i].src = sets[s]["y"][p].data_ptr()
+                    descs[i].bytes = shard
+                    i += 1
+            copy_descs.append(descs)
     if fused:
         # the GEMM epilogue stores every output chunk into every rank's gathered buffer
         for layer in range(layers):
             for s in range(2):
+                # destinations in the order rank, rank + 1, ...: at any moment the ranks store
+                # into different GPUs
                 views[layer][s]["y_copies"] = [
-                    [peer_bufs[dst][s * len(specs) + p] + rank * sp["rows"] * sp["n"] * 2 for dst in range(world)]
+                    [peer_bufs[(rank + q) % world][s * len(specs) + p] + rank * sp["rows"] * sp["n"] * 2
+                     for q in range(world)]
                     for p, sp in enumerate(specs)]
 
     def gather(s: int) -> None:
@@ -1101,6 +1124,13 @@ def run_headline(args) -> None:
         buffers (ordered after the GEMM that wrote them); with the fused gather the GEMM has
         written them already, and only the completion events are recorded."""
         computed[s].record(cs)
+        if sm_gather:
+            gs_copy.wait_event(computed[s])
+            nat.check("ima_copy_many", lib.ima_copy_many(ctypes.byref(copy_descs[s]), len(copy_descs[s]),
+                                                         2 * args.c4_gather_sms, gs_copy.cuda_stream))
+            drained[s].record(gs_copy)
+            sent[s].record(gs_copy)
+            return
         if world == 1 or fused:
             drained[s].record(cs)
             if fused:
@@ -1274,6 +1304,9 @@ def run_headline(args) -> None:
                        "fused into the GEMM epilogue: every output chunk stored into every GPU's gathered buffer "
                        "(CUDA-IPC peer memory, plain NVLink stores), receiver-side completion by interprocess "
                        "events" if fused else
+                       f"one copy kernel per layer (512-byte warp stores into CUDA-IPC peer memory) on "
+                       f"{args.c4_gather_sms} SMs kept from the GEMM, receiver-side completion by interprocess "
+                       f"events" if sm_gather else
                        "copy engines: peer-to-peer copies into CUDA-IPC-shared buffers, receiver-side completion by "
                        "interprocess events"),
             "nvlink_bytes_received_per_gpu_per_step": gather_bytes,
@@ -1314,6 +1347,8 @@ def run_headline(args) -> None:
         "cpu_baseline": cpu,
         "measured_peaks": {k: measured_peaks().get(k) for k in ("hbm_gbs", "bf16_tflops")},
     }
+    if sm_gather:
+        nat.call("ima_set_gemm_sm_limit", 0)
     del stacks, sets, views
     torch.cuda.empty_cache()
     # ---- config 4, Hawkeye replay phase (same partition and gathers) ----
@@ -1522,8 +1557,10 @@ def main() -> None:
     ap.add_argument("--c4-tokens", type=int, default=16384)
     ap.add_argument("--c4-layers", type=int, default=28)
     ap.add_argument("--c4-hawkeye-steps", type=int, default=1)
-    ap.add_argument("--c4-gather", choices=["epilogue", "ce"], default="epilogue",
-                    help="N > 1: gather the outputs from the GEMM epilogue (default) or by copy-engine copies")
+    ap.add_argument("--c4-gather", choices=["ce", "sm", "epilogue"], default="ce",
+                    help="N > 1: gather the outputs by copy-engine copies (default), by a copy kernel on "
+                         "--c4-gather-sms SMs kept from the GEMM, or from the GEMM epilogue")
+    ap.add_argument("--c4-gather-sms", type=int, default=8)
     ap.add_argument("--c1-only", action="store_true", help="only the config-1 measurement (one GPU)")
     ap.add_argument("--profile-c4", action="store_true", help="two eager forwards of --c4-layers layers (for ncu)")
     args = ap.parse_args()

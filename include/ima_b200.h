@@ -76,6 +76,18 @@ int ima_ipc_free(void* ptr);
 int ima_ipc_open(const void* handle, void** ptr);
 int ima_ipc_close(void* ptr);
 int ima_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+/* Up to IMA_COPY_MAX copies in one kernel launch on at most `ctas` thread blocks (512
+ * threads each): the SM-driven counterpart of ima_copy_async for a multi-GPU caller that
+ * keeps a few SMs free of its persistent GEMM (ima_set_gemm_sm_limit) and gathers through
+ * them.  Every warp store is 512 contiguous bytes.  dst and src of every copy must be
+ * 16-byte aligned (IMA_ERR_INVALID_ARGUMENT otherwise); the copies must not overlap. */
+#define IMA_COPY_MAX 128
+typedef struct ima_copy_desc {
+    void* dst;
+    const void* src;
+    int64_t bytes;
+} ima_copy_desc;
+int ima_copy_many(const ima_copy_desc* copies, int count, int ctas, void* stream);
 
 /* ---- A1/A2: per-token FP8 quantiser -----------------------------------------
  * ref: __main__.py:148-154 _per_token_fp8, :157-158 _fp8_e4m3_to_int32,

@@ -65,6 +65,12 @@ class GemmYCopies(ctypes.Structure):
     _fields_ = [("y", _VP * 8)]
 
 
+class CopyDesc(ctypes.Structure):
+    """ima_copy_desc"""
+
+    _fields_ = [("dst", _VP), ("src", _VP), ("bytes", _I64)]
+
+
 class FreivaldsRowsProblem(ctypes.Structure):
     """ima_freivalds_rows_problem"""
 
@@ -91,6 +97,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ima_ipc_open": (_I32, [_VP, _VP]),
     "ima_ipc_close": (_I32, [_VP]),
     "ima_copy_async": (_I32, [_VP, _VP, _I64, _VP]),
+    "ima_copy_many": (_I32, [_VP, _I32, _I32, _VP]),
     "ima_freivalds_weight_vector": (_I32, [_VP, _I64, _VP, _I64, _I64, _VP, _VP]),
     "ima_freivalds_rows_grouped": (_I32, [_VP, _I32, _VP]),
     "ima_status_string": (ctypes.c_char_p, [_I32]),

@@ -110,6 +110,7 @@ struct GemmProblemDev {
     int64_t ldc, ldy;
     int32_t M, N, K, y_dtype;
     int32_t m_tiles, k_tiles, vec_out, ncopy;   // ncopy: extra destinations of y (batch.ycopy)
+    int32_t N_tile, group_m;                    // column tile width (BN); row tiles per group
 };
 
 struct __align__(64) GemmBatch {
@@ -124,6 +125,23 @@ struct __align__(64) GemmBatch {
 
 static_assert(sizeof(GemmBatch) <= 32764, "kernel parameters of one grouped GEMM launch");
 static_assert(GM_MAXD == IMA_GEMM_MAX_Y_COPIES, "copies per problem");
+
+// Tile lt of a problem -> (row tile, column tile).  Row tiles are taken in groups of
+// P.group_m and, within a group, the column tiles in order with the group's row tiles
+// fastest: the tiles in flight at once (one per CTA, consecutive tile numbers) share both
+// the activation and the weight k-slices they stream, and the group's activation planes stay
+// in L2 while its column tiles pass, so the weight planes are read once per group.  (Row
+// tiles fastest over the whole problem would have every column tile stream all the
+// activation planes from DRAM again once they exceed L2.)
+IMA_DEVINL void tile_coords(const GemmProblemDev& P, int64_t lt, int32_t& mt, int32_t& nt) {
+    const int32_t n_tiles = (P.N + (P.N_tile - 1)) / P.N_tile;
+    const int64_t per_group = (int64_t)P.group_m * n_tiles;
+    const int32_t group = (int32_t)(lt / per_group);
+    const int32_t within = (int32_t)(lt - (int64_t)group * per_group);
+    const int32_t gm = min(P.group_m, P.m_tiles - group * P.group_m);
+    mt = group * P.group_m + within % gm;
+    nt = within / gm;
+}
 
 IMA_DEVINL int find_problem(const GemmBatch& b, int64_t t) {
     int lo = 0, hi = b.n - 1;
@@ -194,8 +212,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
             const int pi = find_problem(batch, t);
             const GemmProblemDev& P = batch.p[pi];
             const int64_t lt = t - batch.tile_start[pi];
-            const int32_t m0 = (int32_t)((lt % P.m_tiles) * GM_BM);
-            const int32_t n0 = (int32_t)((lt / P.m_tiles) * BN);
+            int32_t mt, nt;
+            tile_coords(P, lt, mt, nt);
+            const int32_t m0 = mt * GM_BM;
+            const int32_t n0 = nt * BN;
             const CUtensorMap* ma = &batch.maps[pi][0];
             const CUtensorMap* mb = &batch.maps[pi][1];
             for (int kt = 0; kt < P.k_tiles; ++kt) {
@@ -291,8 +311,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
             const int pi = find_problem(batch, t);
             const GemmProblemDev& P = batch.p[pi];
             const int64_t lt = t - batch.tile_start[pi];
-            const int32_t m0 = (int32_t)((lt % P.m_tiles) * GM_BM);
-            const int32_t n0 = (int32_t)((lt / P.m_tiles) * BN) + h * HALF;
+            int32_t mt, nt;
+            tile_coords(P, lt, mt, nt);
+            const int32_t m0 = mt * GM_BM;
+            const int32_t n0 = nt * BN + h * HALF;
             // per-warp copy of this warp's column scales and bias (no cross-warp barrier needed)
             float* ws_t = s_ws + (ew * 2 + (tile_ctr & 1)) * HALF;
             float* bias_t = s_bias + (ew * 2 + (tile_ctr & 1)) * HALF;
@@ -423,10 +445,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1) int_gemm_kernel(const __grid_co
                                 const int64_t off = (gm * P.ldy + gn) * esize;
                                 const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
                                 // y, then each further copy of it (another GPU's gathered
-                                // buffer: plain stores over NVLink)
+                                // buffer: plain stores over NVLink), starting at a different
+                                // copy in each CTA so that the CTAs spread over the destinations
                                 for (int d = -1; d < P.ncopy; ++d) {
+                                    const int dc = d < 0 ? 0 : (int)((d + blockIdx.x) % (uint32_t)P.ncopy);
                                     unsigned char* dst =
-                                        reinterpret_cast<unsigned char*>(d < 0 ? P.y : batch.ycopy[pi][d]) + off;
+                                        reinterpret_cast<unsigned char*>(d < 0 ? P.y : batch.ycopy[pi][dc]) + off;
                                     if (gn + 16 / esize <= P.N) {
                                         *reinterpret_cast<uint4*>(dst) = v;
                                     } else if (esize == 4) {
@@ -526,6 +550,16 @@ int gemm_grid_limit() {
     return (g_gemm_sm_limit > 0 && g_gemm_sm_limit < n) ? g_gemm_sm_limit : n;
 }
 
+// Row tiles per tile group: as many as keep the group's activation planes (GM_BM rows x K
+// bytes x NP planes) within GM_GROUP_BYTES of L2, a power of two in [2, 32].
+constexpr int64_t GM_GROUP_BYTES = 64ll << 20;
+int32_t gemm_group_m(int64_t K, int np) {
+    const int64_t per_tile = (int64_t)GM_BM * std::max<int64_t>(K, 1) * np;
+    int32_t g = 2;
+    while (g < 32 && (int64_t)(2 * g) * per_tile <= GM_GROUP_BYTES) g *= 2;
+    return g;
+}
+
 int check_problem(const ima_gemm_problem& q, int scheme) {
     if (!q.a_planes || !q.b_planes || q.M < 0 || q.N < 0 || q.K < 0) return IMA_ERR_INVALID_ARGUMENT;
     if (!q.c && !q.y) return IMA_ERR_INVALID_ARGUMENT;
@@ -596,6 +630,8 @@ int run_grouped(const ima_gemm_problem* problems, const ima_gemm_y_copies* copie
             D.ldc = q.ldc; D.ldy = q.ldy;
             D.M = (int32_t)q.M; D.N = (int32_t)q.N; D.K = (int32_t)q.K; D.y_dtype = q.y_dtype;
             D.m_tiles = (int32_t)((q.M + GM_BM - 1) / GM_BM);
+            D.N_tile = L::BN;
+            D.group_m = gemm_group_m(q.K, L::NP);
             D.k_tiles = (int32_t)((q.K + GM_KT - 1) / GM_KT);
             // staged 16-byte copy-out needs 16-byte aligned rows; otherwise element stores
             const int yes = q.y_dtype == IMA_DTYPE_F32 ? 4 : 2;

@@ -861,3 +861,32 @@ def test_grouped_gemm_writes_every_copy_of_y(cuda_device):
     arr[1].y = None
     assert lib.ima_int_gemm_grouped_copies(ctypes.byref(arr), ctypes.byref(carr), len(probs),
                                            nat.IMA_SCHEME_DIGITS3, nat.stream_of(cuda_device)) != 0
+
+
+def test_copy_many_moves_every_byte(cuda_device):
+    """ima_copy_many: many copies of ragged sizes (tails shorter than a 16-byte lane and
+    than a 512-byte unit) in one launch on a few blocks; every destination equals its
+    source and nothing around it is touched; misaligned pointers are refused."""
+    import ctypes
+
+    g = torch.Generator().manual_seed(5)
+    sizes = [0, 1, 15, 16, 17, 511, 512, 513, 4096 + 48, 100_000 + 7, 3 * 1024 * 1024 + 16]
+    srcs, dsts = [], []
+    descs = (nat.CopyDesc * len(sizes))()
+    for i, nbytes in enumerate(sizes):
+        src = torch.randint(0, 256, (nbytes + 16,), generator=g, dtype=torch.int64).to(torch.uint8).to(cuda_device)
+        dst = torch.full((nbytes + 32,), 0xA5, dtype=torch.uint8, device=cuda_device)
+        descs[i].dst, descs[i].src, descs[i].bytes = dst.data_ptr() + 16, src.data_ptr(), nbytes
+        srcs.append(src)
+        dsts.append(dst)
+    lib = nat.lib()
+    for ctas in (1, 3, 16):
+        for d in dsts:
+            d.fill_(0xA5)
+        nat.check("copy_many", lib.ima_copy_many(ctypes.byref(descs), len(sizes), ctas, nat.stream_of(cuda_device)))
+        torch.cuda.synchronize()
+        for nbytes, src, dst in zip(sizes, srcs, dsts):
+            assert torch.equal(dst[16:16 + nbytes], src[:nbytes])
+            assert bool((dst[:16] == 0xA5).all()) and bool((dst[16 + nbytes:] == 0xA5).all())
+    descs[3].dst = dsts[3].data_ptr() + 8
+    assert lib.ima_copy_many(ctypes.byref(descs), len(sizes), 4, nat.stream_of(cuda_device)) != 0
