@@ -1049,8 +1049,9 @@ def run_headline(args) -> None:
     cs = torch.cuda.Stream(device)                    # compute
     ms = torch.cuda.Stream(device, priority=-1)       # gather bookkeeping
     gs_copy = torch.cuda.Stream(device, priority=-1)  # copy kernels of the SM gather
-    ce_streams = [torch.cuda.Stream(device, priority=-1) for _ in range(world)]   # one per destination rank
-    ce_done = [[torch.cuda.Event() for _ in range(world)] for _ in range(2)]
+    # copy streams: `--c4-ce-split` per destination rank
+    ce_streams = [torch.cuda.Stream(device, priority=-1) for _ in range(world * args.c4_ce_split)]
+    ce_done = [[torch.cuda.Event() for _ in range(world * args.c4_ce_split)] for _ in range(2)]
     computed = [torch.cuda.Event(), torch.cuda.Event()]
     drained = [torch.cuda.Event(), torch.cuda.Event()]
 
@@ -1136,17 +1137,23 @@ def run_headline(args) -> None:
             if fused:
                 sent[s].record(cs)
             return
+        split = args.c4_ce_split
         for q in range(world):
             dst = (rank + q) % world                  # start at different peers on different ranks
-            st = ce_streams[dst]
-            st.wait_event(computed[s])
-            for p, sp in enumerate(specs):
-                shard = sp["rows"] * sp["n"] * 2
-                nat.call("ima_copy_async", peer_bufs[dst][s * len(specs) + p] + rank * shard, sets[s]["y"][p].data_ptr(),
-                         shard, st.cuda_stream)
-            ce_done[s][q].record(st)
-        for q in range(world):
-            ms.wait_event(ce_done[s][q])
+            for part in range(split):                 # each copy in `split` pieces on as many streams
+                st = ce_streams[dst * split + part]
+                st.wait_event(computed[s])
+                for p, sp in enumerate(specs):
+                    shard = sp["rows"] * sp["n"] * 2
+                    piece = -(-shard // (16 * split)) * 16
+                    lo = part * piece
+                    nbytes = max(0, min(piece, shard - lo))
+                    if nbytes:
+                        nat.call("ima_copy_async", peer_bufs[dst][s * len(specs) + p] + rank * shard + lo,
+                                 sets[s]["y"][p].data_ptr() + lo, nbytes, st.cuda_stream)
+                ce_done[s][q * split + part].record(st)
+        for e in ce_done[s][:world * split]:
+            ms.wait_event(e)
         drained[s].record(ms)
         sent[s].record(ms)
 
@@ -1208,7 +1215,7 @@ def run_headline(args) -> None:
     gather_bytes = sum(2 * (world - 1) * sp["rows"] * sp["n"] for sp in specs) * layers if world > 1 else 0
     int8_peak, peak_source = int8_tensor_peak()
 
-    # ---- timed region: device-resident inputs (2.3 GB of weight planes per layer > L2) ----
+    # ---- timed region: device-resident inputs (2.7 GB of digit planes per layer > L2) ----
     clock = ClockSampler(local)
     clock.start()
     time.sleep(0.3)
@@ -1310,7 +1317,7 @@ def run_headline(args) -> None:
                        "copy engines: peer-to-peer copies into CUDA-IPC-shared buffers, receiver-side completion by "
                        "interprocess events"),
             "nvlink_bytes_received_per_gpu_per_step": gather_bytes,
-            "l2": "inputs larger than L2 (2.3 GB of weight digit planes per layer)",
+            "l2": "inputs larger than L2 (0.70 GB of weight and 2.0 GB of activation digit planes per layer)",
             "activations": "the seven activation matrices of a layer are shared by the 28 layers (the work per "
                            "layer is unchanged)",
         },
@@ -1328,6 +1335,7 @@ def run_headline(args) -> None:
             "gemm_ms_per_step": round(gemm_ms, 3),
             "exact_tops_gemm_only": round(local_ops / (gemm_ms * 1e-3) / 1e12, 2),
             "traffic": fig.get("dram_bytes_per_launch"),
+            "traffic_algorithmic": fig.get("algorithmic_bytes_per_launch"),
             "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one layer's grouped GEMM launch "
                                f"at N = 1 ({fig.get('command')}); capture matches the current source: "
                                f"{fig.get('current')}") if fig else None,
@@ -1561,6 +1569,8 @@ def main() -> None:
                     help="N > 1: gather the outputs by copy-engine copies (default), by a copy kernel on "
                          "--c4-gather-sms SMs kept from the GEMM, or from the GEMM epilogue")
     ap.add_argument("--c4-gather-sms", type=int, default=8)
+    ap.add_argument("--c4-ce-split", type=int, default=1,
+                    help="copy-engine gather: streams per destination rank (each copy split into as many pieces)")
     ap.add_argument("--c1-only", action="store_true", help="only the config-1 measurement (one GPU)")
     ap.add_argument("--profile-c4", action="store_true", help="two eager forwards of --c4-layers layers (for ncu)")
     args = ap.parse_args()
