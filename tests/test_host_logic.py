@@ -370,3 +370,49 @@ def test_plane_cache_keys_on_the_version_counter():
         inf = torch.zeros((4, 8), dtype=torch.int32)
         students._attach_planes(inf, planes)
         assert students._attached_planes(inf) is None
+
+
+def test_codebook_stack_passes_y_copies_to_the_gemm_descriptors():
+    """bufs["y_copies"] (per linear, up to 8 device addresses) lands in the ima_gemm_y_copies
+    array handed to ima_int_gemm_grouped_copies, slot by slot in each launch's problem order;
+    without it the plain grouped launch is used; more than 8 copies are refused."""
+    from types import SimpleNamespace
+
+    from int_model_approximation_b200 import _native as nat
+    from int_model_approximation_b200.pipeline import CodebookStack
+
+    stack = CodebookStack.__new__(CodebookStack)
+    shapes = [(64, 32), (16, 32), (48, 32)]
+    t = lambda *s, dt=torch.float32: torch.zeros(s, dtype=dt)   # noqa: E731
+    stack.linears = [SimpleNamespace(n=n, k=k, w_planes=SimpleNamespace(planes=t(3, n, 32, dt=torch.int8), ld=32),
+                                     w_code_scale=t(n), bias=None, t=t(k, dt=torch.int64), r=t(n, dt=torch.int64))
+                     for n, k in shapes]
+    m = 8
+    bufs = {key: [] for key in ("q", "scale", "code_scale", "planes", "c", "y")}
+    for n, k in shapes:
+        bufs["q"].append(t(m, k, dt=torch.uint8))
+        bufs["scale"].append(t(m))
+        bufs["code_scale"].append(t(m))
+        bufs["planes"].append(SimpleNamespace(planes=t(3, m, 32, dt=torch.int8), ld=32))
+        bufs["c"].append(t(m, n, dt=torch.int64))
+        bufs["y"].append(t(m, n, dt=torch.bfloat16))
+    bufs["mismatch"] = t(1, dt=torch.int32)
+    xs = [t(m, k, dt=torch.bfloat16) for _n, k in shapes]
+    _q, batches, _f = stack._descriptors(xs, bufs)
+    assert all(c_arr is None for _g, _n, c_arr in batches)
+    copies = [[0x1000, 0x2000], [], [0x3000 + 0x100 * d for d in range(8)]]
+    bufs["y_copies"] = copies
+    _q, batches, _f = stack._descriptors(xs, bufs)
+    members = stack._batches()
+    for (g_arr, count, c_arr), mem in zip(batches, members):
+        assert count == len(mem) and c_arr is not None
+        for slot, i in enumerate(mem):
+            got = [c_arr[slot].y[d] or 0 for d in range(8)]
+            assert got == copies[i] + [0] * (8 - len(copies[i]))
+            assert g_arr[slot].y == bufs["y"][i].data_ptr()
+    bufs["y_copies"] = [[1] * 9, [], []]
+    with pytest.raises(ValueError):
+        stack._descriptors(xs, bufs)
+    import ctypes
+
+    assert ctypes.sizeof(nat.GemmYCopies) == 8 * ctypes.sizeof(ctypes.c_void_p)   # ima_gemm_y_copies
